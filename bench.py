@@ -1,0 +1,338 @@
+"""Benchmark of the MiniMax-H3 FP8 attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mh3|reference]
+
+Default arm (``--impl mh3``), N=1: BASELINE config 2 - FP8 self-attention
+forward, B=1 H=40 S=32760 D=128, e4m3 q/k/v with per-(batch, head) scales
+(synthetic N(0,1) with one of 128 channels x8, seed 0), bf16 out.  A step is
+one ``mh3_fp8_attention_fwd`` launch; ``value`` is whole-job TFLOP/s
+(4*B*H*S^2*D per step) with inputs resident in HBM (504 MB of e4m3 inputs,
+larger than the 126 MB L2).  ``e2e`` times the drop-in
+``kernels.fp8_attention.fp8_attention`` on bf16 tensors copied from pinned
+host memory each step, output copied back.
+
+N>1 (torchrun): every rank runs the same single-GPU workload on its own GPU
+(replicas, no collective); ``value`` = all ranks' FLOPs / max-over-ranks time.
+
+``--impl reference``: the reference's CPU implementation of this path
+(``routed_sdpa`` falling back to torch SDPA on CPU tensors,
+kernels/attention_router.py:93-102) on rank 0's host cores, on a bounded
+sample of the same workload (one head, a block of query rows against all
+32760 keys), same metric and unit.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+B, H, S, D = 1, 40, 32760, 128
+FLOP_PER_CALL = 4.0 * B * H * S * S * D
+NOMINAL_FP8_TFLOPS = 4500.0
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            mp = json.load(f)
+        return {"fp8_tflops": 2.0 * float(mp["bf16_tflops"]), "hbm_gbs": float(mp["hbm_gbs"]),
+                "source": "2x measured bf16 dense burst (MEASURED_PEAKS.json)"}
+    except Exception:
+        return {"fp8_tflops": 2.0 * 1590.0, "hbm_gbs": 6650.0, "source": "2x fallback bf16 1.59 PF"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        return dist, dist.get_rank(), ws, local
+    return None, 0, 1, 0
+
+
+def _synthetic_qkv(device, seed=0, dtype=torch.bfloat16):
+    """q, k, v ~ N(0,1) bf16 with one (1% of 128) channel x8 per tensor."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    gc = torch.Generator().manual_seed(seed)
+    out = []
+    for _ in range(3):
+        x = torch.randn(B, H, S, D, generator=g, device=device, dtype=torch.float32)
+        ch = int(torch.randperm(D, generator=gc)[0])
+        x[..., ch] *= 8.0
+        out.append(x.to(dtype))
+        del x
+    return out
+
+
+def _per_bh_e4m3(x):
+    xf = x.float()
+    s = torch.clamp(xf.abs().amax(dim=(2, 3)), min=1e-12) / 448.0
+    x8 = torch.clamp(xf / s[..., None, None], -448, 448).to(torch.float8_e4m3fn)
+    return x8, s[..., None].contiguous()
+
+
+def cpu_reference_sample(seconds: float = 10.0):
+    """The reference's CPU path (torch SDPA fallback) on a bounded sample of config 2."""
+    from oracle.router_ref import cpu_sdpa_fallback
+
+    g = torch.Generator().manual_seed(0)
+    rows = 512
+    q = torch.randn(1, 1, rows, D, generator=g)
+    k = torch.randn(1, 1, S, D, generator=g)
+    v = torch.randn(1, 1, S, D, generator=g)
+    flop = 4.0 * rows * S * D
+    for _ in range(2):
+        cpu_sdpa_fallback(q, k, v)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        cpu_sdpa_fallback(q, k, v)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"value": flop * n / el / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"torch SDPA fp32 on CPU, 1 head x {rows} query rows x {S} keys x D={D}, {n} calls "
+                      f"in {el:.1f}s (the reference's routed_sdpa CPU fallback)"}
+
+
+def run_reference_arm(args, rank):
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    from oracle.router_ref import cpu_sdpa_fallback
+
+    g = torch.Generator().manual_seed(0)
+    rows = 256
+    q = torch.randn(1, 1, rows, D, generator=g)
+    k = torch.randn(1, 1, S, D, generator=g)
+    v = torch.randn(1, 1, S, D, generator=g)
+    flop = 4.0 * rows * S * D
+    for _ in range(max(args.warmup, 1)):
+        cpu_sdpa_fallback(q, k, v)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_sdpa_fallback(q, k, v)
+    el = time.perf_counter() - t0
+    val = flop * args.steps / el / 1e12
+    line = {"metric": "FP8 attention TFLOPS (S=32760 H=40 D=128)", "value": val, "unit": "TFLOP/s",
+            "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config2 sample: 1 head x 256 query rows x 32760 keys, D=128, CPU"},
+            "cpu_baseline": {"value": val, "unit": "TFLOP/s", "kind": "port", "cores": torch.get_num_threads(),
+                             "sample": "torch SDPA fp32 on CPU (routed_sdpa fallback), 1 head x 256 rows x "
+                                       "32760 keys per step"},
+            "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_gpu_arm(args, dist, rank, world, local):
+    from minimaxh3_b200 import ops
+    from minimaxh3_b200.kernels.fp8_attention import fp8_attention
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    q, k, v = _synthetic_qkv(dev)
+    (q8, sq), (k8, sk), (v8, sv) = _per_bh_e4m3(q), _per_bh_e4m3(k), _per_bh_e4m3(v)
+    ls2 = 1.4426950408889634 / math.sqrt(D)
+    out = torch.empty(B, H, S, D, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        ops.attention_e4m3(q8, k8, v8, sq, sk, sv, logit_scale_log2=ls2, out=out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    total_ms = t_start.elapsed_time(t_end)
+    per_launch = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    if dist:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    value = FLOP_PER_CALL * args.steps * world / (total_ms / 1e3) / 1e12
+    avg_launch_ms = sum(per_launch) / len(per_launch)
+    achieved = FLOP_PER_CALL / (avg_launch_ms / 1e3) / 1e12
+    peaks = _peaks()
+
+    # End to end through the drop-in API: pinned host bf16 in, bf16 out back to host.
+    e2e_steps = max(1, min(args.steps, 3))
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    del q, k, v
+    hout = torch.empty((B, H, S, D), dtype=torch.bfloat16).pin_memory()
+    dq, dk, dv = (torch.empty(B, H, S, D, dtype=torch.bfloat16, device=dev) for _ in range(3))
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        o = fp8_attention(dq, dk, dv)
+        hout.copy_(o, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_val = FLOP_PER_CALL * e2e_steps * world / (e2e_ms / 1e3) / 1e12
+    h2d = 3 * B * H * S * D * 2
+    d2h = B * H * S * D * 2
+
+    if rank != 0:
+        return
+    cpu = cpu_reference_sample(seconds=args.cpu_seconds) if world == 1 else None
+    line = {
+        "metric": "FP8 attention TFLOPS (S=32760 H=40 D=128)",
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": total_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "e4m3",
+        "data": "synthetic",
+        "config": {"workload": "config2: FP8 self-attention fwd B=1 H=40 S=32760 D=128, per-(b,h) scales, "
+                               "bf16 out", "inputs_vs_l2": "inputs 504 MB > 126 MB L2 (no flush)",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "pct_of_fp8_peak": achieved / peaks["fp8_tflops"],
+        "pct_of_nominal_fp8_peak": achieved / NOMINAL_FP8_TFLOPS,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["fp8_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / peaks["fp8_tflops"], "traffic": None, "peak_source": peaks["source"],
+                     "kernel": "mh3::attn::fwd_kernel", "avg_launch_ms": avg_launch_ms},
+        "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "minimaxh3_b200.kernels.fp8_attention.fp8_attention (bf16 in/out, quantise + attention)",
+                "steps": e2e_steps},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="mh3", choices=["mh3", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "mh3":
+        args.warmup = 3
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference_arm(args, rank)
+        return
+    dist, rank, world, local = _dist()
+    try:
+        run_gpu_arm(args, dist, rank, world, local)
+    finally:
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,170 @@
+/*
+ * mh3_b200.h - C ABI of the B200 (sm_100a) FP8 attention / FP8 linear hot path
+ * of MiniMax-H3.
+ *
+ * Every entry point takes plain pointers (device memory unless stated),
+ * sizes and strides, and a CUDA stream passed as ``void*`` (a cudaStream_t;
+ * NULL = legacy default stream).  Nothing allocates device memory: outputs
+ * and scratch buffers are owned by the caller.  Calls are asynchronous on
+ * the stream.  Return value: MH3_OK (0) on success; a negative MH3_ERR_*
+ * code for an invalid argument (the message is available from
+ * mh3_last_error() on the calling thread); a positive cudaError_t value if a
+ * CUDA launch failed.
+ *
+ * Element strides are in elements of the tensor's own type; the last
+ * dimension (channels / K) is always contiguous.
+ *
+ * Each entry point names the reference (viragadel6/minimaxh3) interface it
+ * replaces, as path:line.
+ */
+#ifndef MH3_B200_H_
+#define MH3_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define MH3_API
+#else
+#define MH3_API __attribute__((visibility("default")))
+#endif
+
+#define MH3_ABI_VERSION 1
+
+#define MH3_OK 0
+#define MH3_ERR_INVALID (-1)     /* bad argument: shape, stride, alignment, null pointer */
+#define MH3_ERR_UNSUPPORTED (-2) /* valid but not supported by this build (e.g. head_dim) */
+#define MH3_ERR_DRIVER (-3)      /* CUDA driver call failed (tensor map encoding) */
+#define MH3_ERR_TOO_LARGE (-4)   /* size exceeds a fixed limit of the entry point */
+
+#define MH3_DTYPE_BF16 0
+#define MH3_DTYPE_F16 1
+
+/* Device-side error codes written by kernels into an ``err`` word. */
+#define MH3_DEVERR_NONE 0
+#define MH3_DEVERR_WAIT_TIMEOUT 1 /* an mbarrier wait exceeded timeout_ns */
+
+MH3_API int mh3_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+MH3_API const char* mh3_last_error(void);
+
+/* Address of the library's own device error word on the current device
+ * (used when a call passes err = NULL).  Kernels only ever set it from 0 to a
+ * MH3_DEVERR_* code; read and clear it with ordinary copies. */
+MH3_API int* mh3_device_error_word(void);
+
+/* ------------------------------------------------------------------------ */
+/* FP8 attention forward                                                     */
+/* ------------------------------------------------------------------------ */
+/*
+ * Replaces ``_fp8_attn_kernel`` (kernels/fp8_attention.py:190-297) and the
+ * launch at kernels/fp8_attention.py:379-402.
+ *
+ * Non-causal attention over e4m3 inputs:
+ *   logit2[i,j] = (q8[i] . k8[j]) * scale_q[blk(i)] * scale_k[blk(j)]
+ *                 * logit_scale_log2 + key_bias2[j]          (log2 units)
+ *   out[i,d]    = scale_v[d] * sum_j 2^logit2[i,j] v8[j,d] / sum_j 2^logit2[i,j]
+ * blk(i) = i / 128 within the sequence.  A per-(batch, head) scale is a
+ * block stride of 0.  Rows whose keys are all masked produce 0.
+ *
+ * Dense mode (cu_seqlens_q == cu_seqlens_k == NULL): q8 is [B,H,Sq,D],
+ * k8/v8 are [B,H,Sk,D] under the given strides.
+ * Varlen mode: tensors are packed along the token dimension (the ``s``
+ * stride steps one token; the ``b`` stride is ignored); sequence b owns
+ * tokens [cu_seqlens[b], cu_seqlens[b+1]); ``batch`` = number of sequences;
+ * scale/bias ``b`` strides index the sequence.
+ *
+ * key_bias2 (optional): f32 [B, ceil(Sk/128)*128] additive bias in log2
+ * units, -inf for masked keys AND for the padding past Sk; 16-byte aligned.
+ * It carries both the reference's key_mask and key_bias (:256-264).
+ */
+typedef struct mh3_attn_args {
+  int32_t batch, heads, seqlen_q, seqlen_k, head_dim; /* head_dim: 64 or 128 */
+  int32_t out_dtype;                                   /* MH3_DTYPE_BF16 / MH3_DTYPE_F16 */
+  const void* q8;
+  int64_t q_stride_b, q_stride_h, q_stride_s; /* multiples of 16 */
+  const void* k8;
+  int64_t k_stride_b, k_stride_h, k_stride_s;
+  const void* v8;
+  int64_t v_stride_b, v_stride_h, v_stride_s;
+  void* out;
+  int64_t o_stride_b, o_stride_h, o_stride_s; /* multiples of 8 */
+  const float* scale_q;
+  int64_t sq_stride_b, sq_stride_h, sq_stride_blk;
+  const float* scale_k;
+  int64_t sk_stride_b, sk_stride_h, sk_stride_blk;
+  const float* scale_v;
+  int64_t sv_stride_b, sv_stride_h, sv_stride_d;
+  float logit_scale_log2;
+  int32_t max_seqlen_q; /* varlen only */
+  const int32_t* cu_seqlens_q; /* [batch+1] device, or NULL */
+  const int32_t* cu_seqlens_k;
+  int64_t total_q, total_k; /* varlen only: packed token counts */
+  const float* key_bias2;
+  int64_t key_bias2_stride_b;
+  int* err;            /* device error word, or NULL for the library's own */
+  uint64_t timeout_ns; /* bound on every pipeline wait; 0 = 4 s */
+} mh3_attn_args;
+
+MH3_API int mh3_fp8_attention_fwd(const mh3_attn_args* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Q / K / V quantisation for the drop-in bf16/fp16 path                      */
+/* ------------------------------------------------------------------------ */
+/*
+ * Replaces ``_quantize_q_kernel`` (kernels/fp8_attention.py:39-77), the K
+ * channel mean ``k.float().mean(dim=2)`` (:338), ``_quantize_k_kernel``
+ * (:80-119) and ``_quantize_v_kernel`` (:122-170), with the reference's
+ * arithmetic:
+ *   q8 = e4m3(clamp(q*q_premul / sq, +-448)), sq = max(absmax_128rows, 1e-12)/448
+ *   k8 = e4m3(clamp((k-mean_k)/sk, +-448)),    sk per 128 keys likewise
+ *   v8 = e4m3(clamp(v / sv[d], +-448)),        sv[d] = max(absmax over S, 1e-12)/448
+ * Outputs are contiguous: q8 [B,H,Sq,D], k8/v8 [B,H,Sk,D] (v8 in natural
+ * [key, channel] order - the attention kernel needs no transposed copy),
+ * scale_q [B,H,ceil(Sq/128)], scale_k [B,H,ceil(Sk/128)], scale_v and
+ * k_mean [B,H,D].  ``workspace`` must hold mh3_qkv_workspace_bytes() bytes.
+ */
+typedef struct mh3_qkv_quant_args {
+  int32_t batch, heads, seqlen_q, seqlen_k, head_dim;
+  int32_t in_dtype; /* MH3_DTYPE_BF16 / MH3_DTYPE_F16 */
+  const void* q;
+  int64_t q_stride_b, q_stride_h, q_stride_s;
+  const void* k;
+  int64_t k_stride_b, k_stride_h, k_stride_s;
+  const void* v;
+  int64_t v_stride_b, v_stride_h, v_stride_s;
+  float q_premul; /* softmax scale * log2(e) */
+  void* q8;
+  void* k8;
+  void* v8;
+  float* scale_q;
+  float* scale_k;
+  float* scale_v;
+  float* k_mean;
+  void* workspace;
+} mh3_qkv_quant_args;
+
+MH3_API uint64_t mh3_qkv_workspace_bytes(int32_t batch, int32_t heads, int32_t seqlen_k, int32_t head_dim);
+MH3_API int mh3_quantize_qkv(const mh3_qkv_quant_args* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Per-row e4m3 quantisation                                                 */
+/* ------------------------------------------------------------------------ */
+/*
+ * Replaces ``_quantize_rows_kernel`` / ``quantize_rows``
+ * (kernels/fp8_linear.py:8-42): x8[m,:] = e4m3(clamp(x[m,:]/s[m], +-448)),
+ * s[m] = max(absmax(x[m,:]), 1e-12)/448.  x is [M,K] with row stride
+ * x_stride (elements); x8 is contiguous [M,K]; scale is [M] f32.
+ */
+MH3_API int mh3_quantize_rows(const void* x, int64_t x_stride, int32_t in_dtype, int64_t M, int64_t K, void* x8,
+                      float* scale, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MH3_B200_H_ */

@@ -1,0 +1,535 @@
+// FP8 (e4m3) non-causal flash-attention forward for sm_100a.
+//
+// Replaces the reference's ``_fp8_attn_kernel`` (kernels/fp8_attention.py:190-297
+// of viragadel6/minimaxh3).  Same contract: e4m3 Q, K, V with fp32 dequant
+// scales in, bf16/fp16 out, optional per-key mask or bias.  Different
+// machinery:
+//
+//  * one CTA = two 128-row Q tiles sharing every K/V tile, 384 threads:
+//      warps 0-3   softmax warpgroup for Q tile 0 (thread i owns row i)
+//      warps 4-7   softmax warpgroup for Q tile 1
+//      warp  8     TMA producer (K and V tiles through a 3-stage mbarrier ring)
+//      warp  9     tcgen05 MMA issuer; owns the 512-column TMEM allocation
+//      warps 10-11 idle (complete the third warpgroup for setmaxnreg)
+//  * TMEM columns: S0 [0,128)  S1 [128,256)  O0 [256,256+D)  O1 [256+D,256+2D);
+//    P (128x128 e4m3 = 32 columns) is written over the first 32 columns of S.
+//  * S = Q K^T and O += P V are tcgen05.mma kind::f8f6f4 (M=128, K=32 steps).
+//    V stays in its natural [key, channel] layout: the PV MMA reads it as an
+//    MN-major B operand, so no transposed copy of V is ever made.
+//  * MMA order  S0(0) S1(0) | PV0(j) S0(j+1) PV1(j) S1(j+1) ... : the tensor
+//    core works on one Q tile while the other tile's softmax runs.
+//  * softmax: exp2 with the dequant scales folded into one FMA per element,
+//    P = e4m3(2^(s*c - m + P_OFFSET)) via packed f16x2 ex2; the running max m
+//    is raised lazily (only when a tile's max exceeds it by LAZY_T, the idea
+//    of the reference's ``rowmax > m + 8`` at :267), and the rare O rescale is
+//    done in TMEM by the softmax warp itself before it releases P.
+//  * every mbarrier wait is bounded; a timeout sets an error word and lets the
+//    CTA run to teardown (TMEM is always freed, copies in flight drained).
+#include <mutex>
+#include <string>
+
+#include "mh3_b200.h"
+#include "mh3_internal.h"
+#include "ptx.cuh"
+
+namespace mh3 {
+namespace attn {
+
+constexpr int BM = 128;  // rows per Q tile
+constexpr int BN = 128;  // keys per K/V tile
+constexpr int KST = 3;   // K ring depth
+constexpr int VST = 3;   // V ring depth
+constexpr int NUM_THREADS = 384;
+constexpr float LAZY_T = 4.5f;    // lazy max threshold (log2 units)
+constexpr float P_OFFSET = 4.0f;  // P = 2^(x + P_OFFSET) <= 2^(LAZY_T+P_OFFSET) < 448
+
+struct Params {
+  CUtensorMap tmq;  // e4m3 (D, S, H, B), box (D, 128, 1, 1)
+  CUtensorMap tmk;
+  CUtensorMap tmv;
+  void* out;
+  long long osb, osh, oss;  // output strides in elements (d contiguous)
+  const float* sq;
+  long long sqb, sqh, sqblk;
+  const float* sk;
+  long long skb, skh, skblk;
+  const float* sv;
+  long long svb, svh, svd;
+  float logit_scale_log2;
+  int H, Sq, Sk;
+  const int* cuq;  // varlen: cumulative sequence starts (B+1), or null
+  const int* cuk;
+  const float* kbias2;  // additive per-key bias in log2 units, [B, ceil(Sk/128)*128], or null
+  long long kbias_sb;
+  int* err;
+  unsigned long long timeout_ns;
+};
+
+template <int D>
+struct __align__(1024) Smem {
+  uint8_t q[2][BM * D];
+  uint8_t k[KST][BN * D];
+  uint8_t v[VST][BN * D];
+  uint64_t bar_q;
+  uint64_t bar_kfull[KST];
+  uint64_t bar_kempty[KST];
+  uint64_t bar_vfull[VST];
+  uint64_t bar_vempty[VST];
+  uint64_t bar_s[2];
+  uint64_t bar_p[2];
+  uint64_t bar_o;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+template <int D>
+constexpr uint32_t smem_bytes() {
+  return (uint32_t)sizeof(Smem<D>) + 1024;
+}
+
+__device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
+__device__ __forceinline__ uint32_t f2u(float x) { return __float_as_uint(x); }
+
+template <int D, bool OUT_F16, bool HAS_BIAS>
+__global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem<D>& sm = *reinterpret_cast<Smem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+
+  int q_start = 0, q_len = p.Sq, k_start = 0, k_len = p.Sk, bcoord = b;
+  if (p.cuq != nullptr) {
+    q_start = p.cuq[b];
+    q_len = p.cuq[b + 1] - q_start;
+    k_start = p.cuk[b];
+    k_len = p.cuk[b + 1] - k_start;
+    bcoord = 0;
+  }
+  const int qt0 = blockIdx.x * 2;
+  if (qt0 * BM >= q_len) return;  // uniform over the CTA, before any barrier
+  const int nk = (k_len + BN - 1) / BN;
+
+  // Swizzle-128B (D=128) or swizzle-64B (D=64) tiles: row = D bytes.
+  constexpr uint32_t kLayout = (D == 128) ? kLayoutSW128 : kLayoutSW64;
+  constexpr uint32_t kRowBytes = D;
+  constexpr uint32_t kTileBytes = BN * D;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&sm.bar_q), 1);
+    for (int i = 0; i < KST; ++i) {
+      mbar_init(smem_u32(&sm.bar_kfull[i]), 1);
+      mbar_init(smem_u32(&sm.bar_kempty[i]), 1);
+    }
+    for (int i = 0; i < VST; ++i) {
+      mbar_init(smem_u32(&sm.bar_vfull[i]), 1);
+      mbar_init(smem_u32(&sm.bar_vempty[i]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&sm.bar_s[i]), 1);
+      mbar_init(smem_u32(&sm.bar_p[i]), 4);
+    }
+    mbar_init(smem_u32(&sm.bar_o), 1);
+    sm.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(&sm.tmem_base), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  const WaitGuard g{&sm.abort_flag, p.err, p.timeout_ns};
+
+  if (warp >= 8) {
+    setmaxnreg_dec<64>();
+    if (warp == 8 && lane == 0) {
+      // ---------------------------------------------------------------- producer
+      tma_prefetch_desc(&p.tmq);
+      tma_prefetch_desc(&p.tmk);
+      tma_prefetch_desc(&p.tmv);
+      const uint32_t bq = smem_u32(&sm.bar_q);
+      mbar_arrive_expect_tx(bq, 2 * BM * D);
+      tma_load_4d(smem_u32(sm.q[0]), &p.tmq, bq, 0, q_start + qt0 * BM, h, bcoord);
+      tma_load_4d(smem_u32(sm.q[1]), &p.tmq, bq, 0, q_start + (qt0 + 1) * BM, h, bcoord);
+      int issued = 0;
+      for (int j = 0; j < nk; ++j) {
+        const int ks = j % KST;
+        const uint32_t kph = (uint32_t)(j / KST) & 1u;
+        if (!mbar_wait(smem_u32(&sm.bar_kempty[ks]), kph ^ 1u, g)) break;
+        mbar_arrive_expect_tx(smem_u32(&sm.bar_kfull[ks]), kTileBytes);
+        tma_load_4d(smem_u32(sm.k[ks]), &p.tmk, smem_u32(&sm.bar_kfull[ks]), 0, k_start + j * BN, h, bcoord);
+        const int vs = j % VST;
+        const uint32_t vph = (uint32_t)(j / VST) & 1u;
+        if (!mbar_wait(smem_u32(&sm.bar_vempty[vs]), vph ^ 1u, g)) {
+          issued = -(j + 1);  // K(j) issued, V(j) not
+          break;
+        }
+        mbar_arrive_expect_tx(smem_u32(&sm.bar_vfull[vs]), kTileBytes);
+        tma_load_4d(smem_u32(sm.v[vs]), &p.tmv, smem_u32(&sm.bar_vfull[vs]), 0, k_start + j * BN, h, bcoord);
+        issued = j + 1;
+      }
+      // Teardown: let the last copy issued into each stage land before exit.
+      const int nk_issued = issued >= 0 ? issued : -issued;
+      const int nv_issued = issued >= 0 ? issued : -issued - 1;
+      mbar_wait_teardown(bq, 0, p.timeout_ns);
+      for (int j = (nk_issued > KST ? nk_issued - KST : 0); j < nk_issued; ++j)
+        mbar_wait_teardown(smem_u32(&sm.bar_kfull[j % KST]), (uint32_t)(j / KST) & 1u, p.timeout_ns);
+      for (int j = (nv_issued > VST ? nv_issued - VST : 0); j < nv_issued; ++j)
+        mbar_wait_teardown(smem_u32(&sm.bar_vfull[j % VST]), (uint32_t)(j / VST) & 1u, p.timeout_ns);
+    } else if (warp == 9 && lane == 0) {
+      // ---------------------------------------------------------------- MMA issuer
+      constexpr uint32_t kIdescS = idesc_e4m3(BM, BN, false, false);
+      constexpr uint32_t kIdescO = idesc_e4m3(BM, D, false, true);
+      const uint32_t tS[2] = {tmem + 0u, tmem + 128u};
+      const uint32_t tO[2] = {tmem + 256u, tmem + 256u + (uint32_t)D};
+      const uint32_t q_base[2] = {smem_u32(sm.q[0]), smem_u32(sm.q[1])};
+      // K-major operands (Q, K): 8-row swizzle atoms of D bytes per row, K
+      // advanced 32 bytes (32 e4m3) per MMA.  MN-major V: one swizzle atom
+      // across D channels, 8-key groups D*8 bytes apart, 32 keys per MMA.
+      auto kmaj = [&](uint32_t base, int kk) { return smem_desc(base + kk * 32, 16, 8 * kRowBytes, kLayout); };
+      auto vdesc = [&](int vs, int kk) {
+        return smem_desc(smem_u32(sm.v[vs]) + kk * 32 * kRowBytes, kTileBytes, 8 * kRowBytes, kLayout);
+      };
+      auto issue_s = [&](int t, int ks) {
+        const uint32_t kb = smem_u32(sm.k[ks]);
+#pragma unroll
+        for (int kk = 0; kk < D / 32; ++kk) mma_f8_ss(tS[t], kmaj(q_base[t], kk), kmaj(kb, kk), kIdescS, kk > 0);
+      };
+      bool ok = mbar_wait(smem_u32(&sm.bar_q), 0, g);
+      if (nk > 0) {
+        ok = mbar_wait(smem_u32(&sm.bar_kfull[0]), 0, g) && ok;
+        tc_fence_after();
+        issue_s(0, 0);
+        mma_commit(smem_u32(&sm.bar_s[0]));
+        issue_s(1, 0);
+        mma_commit(smem_u32(&sm.bar_s[1]));
+        mma_commit(smem_u32(&sm.bar_kempty[0]));
+      }
+      for (int j = 0; j < nk; ++j) {
+        const int vs = j % VST;
+        mbar_wait(smem_u32(&sm.bar_vfull[vs]), (uint32_t)(j / VST) & 1u, g);
+        const int ks = (j + 1) % KST;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          mbar_wait(smem_u32(&sm.bar_p[t]), (uint32_t)j & 1u, g);
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BN / 32; ++kk)
+            mma_f8_ts(tO[t], tS[t] + (uint32_t)(kk * 8), vdesc(vs, kk), kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+          if (t == 1) mma_commit(smem_u32(&sm.bar_vempty[vs]));
+          if (j + 1 < nk) {
+            if (t == 0) {
+              mbar_wait(smem_u32(&sm.bar_kfull[ks]), (uint32_t)((j + 1) / KST) & 1u, g);
+              tc_fence_after();
+            }
+            issue_s(t, ks);
+            mma_commit(smem_u32(&sm.bar_s[t]));
+            if (t == 1) mma_commit(smem_u32(&sm.bar_kempty[ks]));
+          }
+        }
+      }
+      mma_commit(smem_u32(&sm.bar_o));
+      (void)ok;
+      // Every MMA must be finished before the CTA frees TMEM.
+      mbar_wait_teardown(smem_u32(&sm.bar_o), 0, p.timeout_ns);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax
+    setmaxnreg_inc<216>();
+    const int t = warp >> 2;
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+    const uint32_t tS = tmem + (uint32_t)(t * 128) + lane_off;
+    const uint32_t tO = tmem + 256u + (uint32_t)(t * D) + lane_off;
+    const int qt = qt0 + t;
+    const bool tile_live = qt * BM < q_len;
+    const float sq = tile_live ? __ldg(p.sq + b * p.sqb + h * p.sqh + (long long)qt * p.sqblk) : 1.0f;
+    const float cq = p.logit_scale_log2 * sq;
+    const float* skp = p.sk + b * p.skb + h * p.skh;
+    const float* biasp = HAS_BIAS ? (p.kbias2 + b * p.kbias_sb) : nullptr;
+
+    float m = -1.0e30f;  // running max (log2 units), raised lazily
+    float l = 0.0f;      // running sum of 2^(x + P_OFFSET)
+    for (int j = 0; j < nk; ++j) {
+      mbar_wait(smem_u32(&sm.bar_s[t]), (uint32_t)j & 1u, g);
+      tc_fence_after();
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tS + (uint32_t)(c * 32), sr[c]);
+      tmem_wait_ld();
+
+      const float c_tile = cq * __ldg(skp + (long long)j * p.skblk);
+      float tmax;
+      float2 cc;
+      if constexpr (HAS_BIAS) {
+        // t = s*c + bias2 (bias2 = -inf for masked or padding keys)
+        const float4* bp = reinterpret_cast<const float4*>(biasp + (long long)j * BN);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 bb = __ldg(bp + c * 8 + i);
+            sr[c][4 * i + 0] = f2u(fmaf(u2f(sr[c][4 * i + 0]), c_tile, bb.x));
+            sr[c][4 * i + 1] = f2u(fmaf(u2f(sr[c][4 * i + 1]), c_tile, bb.y));
+            sr[c][4 * i + 2] = f2u(fmaf(u2f(sr[c][4 * i + 2]), c_tile, bb.z));
+            sr[c][4 * i + 3] = f2u(fmaf(u2f(sr[c][4 * i + 3]), c_tile, bb.w));
+          }
+        }
+        cc = make_float2(1.0f, 1.0f);
+      } else {
+        const int rem = k_len - j * BN;
+        if (rem < BN) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (c * 32 + i >= rem) sr[c][i] = f2u(-INFINITY);
+        }
+        cc = make_float2(c_tile, c_tile);
+      }
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        mx0 = fmax3(mx0, u2f(sr[0][i]), u2f(sr[0][i + 1]));
+        mx1 = fmax3(mx1, u2f(sr[1][i]), u2f(sr[1][i + 1]));
+        mx2 = fmax3(mx2, u2f(sr[2][i]), u2f(sr[2][i + 1]));
+        mx3 = fmax3(mx3, u2f(sr[3][i]), u2f(sr[3][i + 1]));
+      }
+      float rmax = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      tmax = HAS_BIAS ? rmax : rmax * c_tile;
+
+      const bool upd = tmax > m + LAZY_T;
+      const float m_new = upd ? tmax : m;
+      const float alpha = ex2_approx(m - m_new);  // 1 when not raised, 0 from the initial sentinel
+      if (j > 0 && __any_sync(0xffffffffu, upd)) {
+        // Rescale this row of O in TMEM.  PV(j-1) has completed: the commit
+        // behind bar_s(j) tracks every MMA issued before S(j).
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + (uint32_t)(c * 32), o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = f2u(u2f(o[i]) * alpha);
+          tmem_st32(tO + (uint32_t)(c * 32), o);
+        }
+      }
+      l *= alpha;
+      m = m_new;
+
+      const float nb = P_OFFSET - m;
+      const float2 nn = make_float2(nb, nb);
+      uint32_t pk[32];
+      float lsum = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t hacc = 0u;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 x = ffma2(make_float2(u2f(sr[c][2 * i]), u2f(sr[c][2 * i + 1])), cc, nn);
+          const uint32_t e = ex2_f16x2(cvt_f16x2(x.y, x.x));
+          hacc = hadd2(hacc, e);
+          const uint32_t p2 = cvt_e4m3x2_f16x2(e);
+          if (i & 1)
+            pk[c * 8 + (i >> 1)] |= p2 << 16;
+          else
+            pk[c * 8 + (i >> 1)] = p2;
+        }
+        const float2 hs = f16x2_to_float2(hacc);
+        lsum += hs.x + hs.y;
+      }
+      l += lsum;
+      tmem_st32(tS, pk);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sm.bar_p[t]));
+    }
+
+    // ---------------------------------------------------------------- epilogue
+    const int grow = qt * BM + row;
+    const bool row_ok = grow < q_len;
+    using OutT = typename std::conditional<OUT_F16, __half, __nv_bfloat16>::type;
+    OutT* orow = reinterpret_cast<OutT*>(p.out) + b * p.osb + h * p.osh + (long long)(q_start + grow) * p.oss;
+    const float* svp = p.sv + b * p.svb + h * p.svh;
+    if (nk > 0) {
+      mbar_wait(smem_u32(&sm.bar_o), 0, g);
+      tc_fence_after();
+    }
+    const float inv_l = 1.0f / fmaxf(l, 1.0e-30f);
+#pragma unroll
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t o[32];
+      if (nk > 0) {
+        tmem_ld32(tO + (uint32_t)(c * 32), o);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = 0u;
+      }
+      uint32_t packed[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int d0 = c * 32 + 2 * i;
+        const float a0 = u2f(o[2 * i]) * __ldg(svp + d0 * p.svd) * inv_l;
+        const float a1 = u2f(o[2 * i + 1]) * __ldg(svp + (d0 + 1) * p.svd) * inv_l;
+        if constexpr (OUT_F16) {
+          __half2 hv = __floats2half2_rn(a0, a1);
+          packed[i] = *reinterpret_cast<uint32_t*>(&hv);
+        } else {
+          __nv_bfloat162 hv = __floats2bfloat162_rn(a0, a1);
+          packed[i] = *reinterpret_cast<uint32_t*>(&hv);
+        }
+      }
+      if (row_ok) {
+        uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------------
+
+static int make_map(CUtensorMap* map, const void* base, int D, long long S, int H, int B, long long ss,
+                    long long sh, long long sb) {
+  // dims (D, S, H, B) innermost first; strides in bytes for dims 1..3.
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)ss, (cuuint64_t)sh, (cuuint64_t)sb};
+  const cuuint32_t box[4] = {(cuuint32_t)D, (cuuint32_t)BN, 1u, 1u};
+  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  const CUtensorMapSwizzle sw = (D == 128) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  return encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, box, estr,
+                      sw);
+}
+
+template <int D, bool F16, bool BIAS>
+static cudaError_t launch(const Params& p, dim3 grid, cudaStream_t st) {
+  auto kern = fwd_kernel<D, F16, BIAS>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes<D>());
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  kern<<<grid, NUM_THREADS, smem_bytes<D>(), st>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace attn
+}  // namespace mh3
+
+using namespace mh3;
+
+extern "C" int mh3_fp8_attention_fwd(const mh3_attn_args* a, void* stream) {
+  if (a == nullptr) return fail(MH3_ERR_INVALID, "mh3_fp8_attention_fwd: null args");
+  const int D = a->head_dim;
+  if (D != 64 && D != 128) return fail(MH3_ERR_INVALID, "head_dim must be 64 or 128");
+  if (a->batch <= 0 || a->heads <= 0) return fail(MH3_ERR_INVALID, "batch and heads must be positive");
+  const bool varlen = a->cu_seqlens_q != nullptr || a->cu_seqlens_k != nullptr;
+  if (varlen && (a->cu_seqlens_q == nullptr || a->cu_seqlens_k == nullptr))
+    return fail(MH3_ERR_INVALID, "varlen needs both cu_seqlens_q and cu_seqlens_k");
+  if (varlen && a->max_seqlen_q <= 0) return fail(MH3_ERR_INVALID, "varlen needs max_seqlen_q > 0");
+  if (!varlen && (a->seqlen_q <= 0 || a->seqlen_k <= 0))
+    return fail(MH3_ERR_INVALID, "seqlen_q and seqlen_k must be positive");
+  if (!a->q8 || !a->k8 || !a->v8 || !a->out || !a->scale_q || !a->scale_k || !a->scale_v)
+    return fail(MH3_ERR_INVALID, "null tensor pointer");
+  if (a->out_dtype != MH3_DTYPE_BF16 && a->out_dtype != MH3_DTYPE_F16)
+    return fail(MH3_ERR_INVALID, "out_dtype must be bf16 or f16");
+  // TMA: 16-byte aligned bases and strides; output rows written as 16-byte vectors.
+  auto al16 = [](const void* p_) { return ((uintptr_t)p_ & 15u) == 0; };
+  if (!al16(a->q8) || !al16(a->k8) || !al16(a->v8) || !al16(a->out))
+    return fail(MH3_ERR_INVALID, "q8/k8/v8/out must be 16-byte aligned");
+  const long long qs[3] = {a->q_stride_s, a->q_stride_h, a->q_stride_b};
+  const long long ks[3] = {a->k_stride_s, a->k_stride_h, a->k_stride_b};
+  const long long vs[3] = {a->v_stride_s, a->v_stride_h, a->v_stride_b};
+  for (int i = 0; i < 3; ++i) {
+    if ((qs[i] % 16) || (ks[i] % 16) || (vs[i] % 16))
+      return fail(MH3_ERR_INVALID, "q8/k8/v8 strides must be multiples of 16 elements");
+  }
+  if ((a->o_stride_s % 8) || (a->o_stride_h % 8) || (a->o_stride_b % 8))
+    return fail(MH3_ERR_INVALID, "output strides must be multiples of 8 elements");
+  if (a->key_bias2 != nullptr && (((uintptr_t)a->key_bias2 & 15u) || (a->key_bias2_stride_b % 4)))
+    return fail(MH3_ERR_INVALID, "key_bias2 must be 16-byte aligned with a row stride multiple of 4");
+
+  attn::Params p;
+  memset(&p, 0, sizeof(p));
+  const int B = a->batch, H = a->heads;
+  const long long Sq_dim = varlen ? a->total_q : a->seqlen_q;
+  const long long Sk_dim = varlen ? a->total_k : a->seqlen_k;
+  if (varlen && (Sq_dim <= 0 || Sk_dim <= 0)) return fail(MH3_ERR_INVALID, "varlen needs total_q/total_k > 0");
+  const int Bdim = varlen ? 1 : B;
+  int rc = attn::make_map(&p.tmq, a->q8, D, Sq_dim, H, Bdim, a->q_stride_s, a->q_stride_h,
+                          varlen ? Sq_dim * a->q_stride_s : a->q_stride_b);
+  if (rc) return rc;
+  rc = attn::make_map(&p.tmk, a->k8, D, Sk_dim, H, Bdim, a->k_stride_s, a->k_stride_h,
+                      varlen ? Sk_dim * a->k_stride_s : a->k_stride_b);
+  if (rc) return rc;
+  rc = attn::make_map(&p.tmv, a->v8, D, Sk_dim, H, Bdim, a->v_stride_s, a->v_stride_h,
+                      varlen ? Sk_dim * a->v_stride_s : a->v_stride_b);
+  if (rc) return rc;
+  p.out = a->out;
+  p.osb = a->o_stride_b;
+  p.osh = a->o_stride_h;
+  p.oss = a->o_stride_s;
+  p.sq = a->scale_q;
+  p.sqb = a->sq_stride_b;
+  p.sqh = a->sq_stride_h;
+  p.sqblk = a->sq_stride_blk;
+  p.sk = a->scale_k;
+  p.skb = a->sk_stride_b;
+  p.skh = a->sk_stride_h;
+  p.skblk = a->sk_stride_blk;
+  p.sv = a->scale_v;
+  p.svb = a->sv_stride_b;
+  p.svh = a->sv_stride_h;
+  p.svd = a->sv_stride_d;
+  p.logit_scale_log2 = a->logit_scale_log2;
+  p.H = H;
+  p.Sq = a->seqlen_q;
+  p.Sk = a->seqlen_k;
+  p.cuq = a->cu_seqlens_q;
+  p.cuk = a->cu_seqlens_k;
+  p.kbias2 = a->key_bias2;
+  p.kbias_sb = a->key_bias2_stride_b;
+  p.err = a->err ? a->err : device_error_word();
+  p.timeout_ns = a->timeout_ns ? a->timeout_ns : 4000000000ull;
+
+  const int max_q = varlen ? a->max_seqlen_q : a->seqlen_q;
+  const int q_tiles = (max_q + attn::BM - 1) / attn::BM;
+  const dim3 grid((unsigned)((q_tiles + 1) / 2), (unsigned)H, (unsigned)B);
+  if (grid.y > 65535u || grid.z > 65535u) return fail(MH3_ERR_INVALID, "too many heads or batches");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const bool f16 = a->out_dtype == MH3_DTYPE_F16;
+  const bool bias = a->key_bias2 != nullptr;
+  cudaError_t e;
+  if (D == 128) {
+    if (f16)
+      e = bias ? attn::launch<128, true, true>(p, grid, st) : attn::launch<128, true, false>(p, grid, st);
+    else
+      e = bias ? attn::launch<128, false, true>(p, grid, st) : attn::launch<128, false, false>(p, grid, st);
+  } else {
+    if (f16)
+      e = bias ? attn::launch<64, true, true>(p, grid, st) : attn::launch<64, true, false>(p, grid, st);
+    else
+      e = bias ? attn::launch<64, false, true>(p, grid, st) : attn::launch<64, false, false>(p, grid, st);
+  }
+  if (e != cudaSuccess) return fail_cuda(e, "mh3_fp8_attention_fwd launch");
+  return MH3_OK;
+}

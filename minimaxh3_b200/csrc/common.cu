@@ -1,0 +1,76 @@
+// Host-side helpers of libmh3_b200: error reporting, tensor-map encoding,
+// the library's device error word.
+#include <mutex>
+#include <string>
+
+#include "mh3_internal.h"
+
+namespace mh3 {
+
+static thread_local std::string g_last_error;
+
+int fail(int code, const char* msg) {
+  g_last_error = msg ? msg : "";
+  return code;
+}
+
+int fail_cuda(cudaError_t e, const char* what) {
+  g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+  return (int)e;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, void* base, const cuuint64_t* dims,
+                 const cuuint64_t* strides_bytes, const cuuint32_t* box, const cuuint32_t* elem_strides,
+                 CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = get_encode();
+  if (fn == nullptr) return fail(MH3_ERR_DRIVER, "cuTensorMapEncodeTiled entry point unavailable");
+  CUresult r = fn(map, dtype, rank, base, dims, strides_bytes, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    std::string msg = "cuTensorMapEncodeTiled failed (CUresult " + std::to_string((int)r) + ")";
+    return fail(MH3_ERR_DRIVER, msg.c_str());
+  }
+  return MH3_OK;
+}
+
+// One error word per device, in the module's global memory.
+__device__ int g_device_error;
+
+int* device_error_word() {
+  constexpr int kMaxDevices = 64;
+  static int* addr[kMaxDevices] = {};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) == cudaSuccess) addr[dev] = static_cast<int*>(p);
+  }
+  return addr[dev];
+}
+
+}  // namespace mh3
+
+extern "C" int mh3_abi_version(void) { return MH3_ABI_VERSION; }
+
+extern "C" const char* mh3_last_error(void) { return mh3::g_last_error.c_str(); }
+
+extern "C" int* mh3_device_error_word(void) { return mh3::device_error_word(); }

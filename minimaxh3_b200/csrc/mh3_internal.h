@@ -1,0 +1,31 @@
+// Host-side helpers shared by the translation units of libmh3_b200.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <type_traits>
+
+#include "mh3_b200.h"
+
+namespace mh3 {
+
+// Record ``msg`` as this thread's last error and return ``code``.
+int fail(int code, const char* msg);
+// Record a CUDA error with context and return it as a positive code.
+int fail_cuda(cudaError_t e, const char* what);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// dependency on libcuda).  Returns MH3_OK or MH3_ERR_DRIVER.
+int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, void* base, const cuuint64_t* dims,
+                 const cuuint64_t* strides_bytes, const cuuint32_t* box, const cuuint32_t* elem_strides,
+                 CUtensorMapSwizzle swizzle);
+
+// The library's device error word on the current device.
+int* device_error_word();
+
+}  // namespace mh3

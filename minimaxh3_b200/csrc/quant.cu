@@ -1,0 +1,304 @@
+// e4m3 quantisation kernels (HBM-bound, CUDA cores).
+//
+//  * mh3_quantize_qkv: the drop-in path's Q/K/V quantisation, with the
+//    reference's arithmetic (kernels/fp8_attention.py:39-170, :338).  The
+//    reference walks each (b,h)'s V serially in one program (40 programs at
+//    H=40, :122-170) and materialises an fp32 copy of K for its mean (:338);
+//    here one grid-wide pass gathers per-chunk K sums and V absmax, a small
+//    kernel finishes them in a fixed order (deterministic), and one 128-row
+//    block per CTA is quantised for each of Q, K and V.
+//  * mh3_quantize_rows: per-row scales for the FP8 linear
+//    (kernels/fp8_linear.py:8-42).
+//
+// Divisions are IEEE round-to-nearest (``__fdiv_rn``) and the e4m3 cast is
+// RNE after the same +-448 clamp, so the bytes match the CPU restatement.
+#include "mh3_internal.h"
+#include "ptx.cuh"
+
+namespace mh3 {
+namespace quant {
+
+constexpr int kThreads = 256;
+constexpr int kBlockRows = 128;  // rows per scale block (fp8_attention.py:52, :93)
+constexpr int kStatRows = 256;   // rows per K/V statistics chunk
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&x)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (std::is_same<T, __half>::value) {
+      const __half2 h2 = *reinterpret_cast<const __half2*>(&w[i]);
+      const float2 f = __half22float2(h2);
+      x[2 * i] = f.x;
+      x[2 * i + 1] = f.y;
+    } else {
+      const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+      const float2 f = __bfloat1622float2(h2);
+      x[2 * i] = f.x;
+      x[2 * i + 1] = f.y;
+    }
+  }
+}
+
+__device__ __forceinline__ float clamp448(float x) { return fminf(fmaxf(x, -448.0f), 448.0f); }
+
+// 8 floats -> 8 e4m3 bytes (element 0 in the lowest byte).
+__device__ __forceinline__ uint2 pack8_e4m3(const float (&y)[8]) {
+  uint32_t lo = cvt_e4m3x2_f32(y[1], y[0]) | (cvt_e4m3x2_f32(y[3], y[2]) << 16);
+  uint32_t hi = cvt_e4m3x2_f32(y[5], y[4]) | (cvt_e4m3x2_f32(y[7], y[6]) << 16);
+  return make_uint2(lo, hi);
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[warp] = v;
+  __syncthreads();
+  float r = red[0];
+#pragma unroll
+  for (int i = 1; i < kThreads / 32; ++i) r = fmaxf(r, red[i]);
+  return r;
+}
+
+// Per-chunk column sums of K and column absmax of V.
+// part layout: [B*H, nchunk, D] (sums) and the same for absmax.
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads) kv_stats_kernel(const T* __restrict__ k, long long ksb, long long ksh,
+                                                            long long kss, const T* __restrict__ v, long long vsb,
+                                                            long long vsh, long long vss, int S, int H,
+                                                            float* __restrict__ part_sum,
+                                                            float* __restrict__ part_amax) {
+  constexpr int CG = D / 8;           // column groups of 8 channels
+  constexpr int RL = kThreads / CG;   // row lanes
+  __shared__ float s_sum[RL][D];
+  __shared__ float s_max[RL][D];
+  const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int cg = threadIdx.x % CG, rl = threadIdx.x / CG;
+  const int r_begin = chunk * kStatRows;
+  const int r_end = min(S, r_begin + kStatRows);
+  const T* kp = k + b * ksb + h * ksh + cg * 8;
+  const T* vp = v + b * vsb + h * vsh + cg * 8;
+  float sum[8], amax[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) sum[i] = 0.0f, amax[i] = 0.0f;
+  for (int r = r_begin + rl; r < r_end; r += RL) {
+    float xk[8], xv[8];
+    load8(kp + (long long)r * kss, xk);
+    load8(vp + (long long)r * vss, xv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      sum[i] += xk[i];
+      amax[i] = fmaxf(amax[i], fabsf(xv[i]));
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    s_sum[rl][cg * 8 + i] = sum[i];
+    s_max[rl][cg * 8 + i] = amax[i];
+  }
+  __syncthreads();
+  const int nchunk = gridDim.x;
+  for (int d = threadIdx.x; d < D; d += kThreads) {
+    float a = 0.0f, m = 0.0f;
+    for (int i = 0; i < RL; ++i) {
+      a += s_sum[i][d];
+      m = fmaxf(m, s_max[i][d]);
+    }
+    const long long o = ((long long)(b * H + h) * nchunk + chunk) * D + d;
+    part_sum[o] = a;
+    part_amax[o] = m;
+  }
+}
+
+// k_mean = sum / S and scale_v = max(absmax, 1e-12) / 448, chunks in order.
+template <int D>
+__global__ void kv_finalize_kernel(const float* __restrict__ part_sum, const float* __restrict__ part_amax,
+                                   int nchunk, int S, float* __restrict__ k_mean, float* __restrict__ scale_v) {
+  const int bh = blockIdx.x;
+  const int d = threadIdx.x;
+  if (d >= D) return;
+  float a = 0.0f, m = 0.0f;
+  for (int c = 0; c < nchunk; ++c) {
+    const long long o = ((long long)bh * nchunk + c) * D + d;
+    a += part_sum[o];
+    m = fmaxf(m, part_amax[o]);
+  }
+  k_mean[(long long)bh * D + d] = a / (float)S;
+  scale_v[(long long)bh * D + d] = fmaxf(m, 1.0e-12f) / 448.0f;
+}
+
+enum Mode { kQ = 0, kK = 1, kV = 2 };
+
+// One 128-row block of one (b, h): transform, block absmax (Q, K), divide,
+// clamp, e4m3.  Output contiguous [B,H,S,D]; scale [B,H,nblk].
+template <typename T, int D, int MODE>
+__global__ void __launch_bounds__(kThreads) block_quant_kernel(const T* __restrict__ x, long long sb, long long sh,
+                                                               long long ss, int S, int H, float premul,
+                                                               const float* __restrict__ chan /* mean or sv */,
+                                                               uint8_t* __restrict__ out, float* __restrict__ scale) {
+  constexpr int CG = D / 8;
+  constexpr int RL = kThreads / CG;
+  constexpr int R = kBlockRows / RL;  // rows per thread
+  __shared__ float red[kThreads / 32];
+  const int blk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int nblk = (S + kBlockRows - 1) / kBlockRows;
+  if (blk >= nblk) return;
+  const int cg = threadIdx.x % CG, rl = threadIdx.x / CG;
+  const T* xp = x + b * sb + h * sh + cg * 8;
+  const long long bh = (long long)b * H + h;
+  float c8[8];
+  if (MODE != kQ) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) c8[i] = chan[bh * D + cg * 8 + i];
+  }
+  float v[R][8];
+  float amax = 0.0f;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int row = blk * kBlockRows + rl + r * RL;
+    if (row < S) {
+      load8(xp + (long long)row * ss, v[r]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (MODE == kQ) v[r][i] = v[r][i] * premul;   // fp8_attention.py:69
+        if (MODE == kK) v[r][i] = v[r][i] - c8[i];    // :111
+        amax = fmaxf(amax, fabsf(v[r][i]));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[r][i] = 0.0f;     // masked rows are 0 (:69, :111)
+    }
+  }
+  float s = 1.0f;
+  if (MODE != kV) {
+    const float bm = block_max(amax, red);             // :70, :112
+    s = fmaxf(bm, 1.0e-12f) / 448.0f;                  // :71, :113
+    if (threadIdx.x == 0) scale[bh * nblk + blk] = s;
+  }
+  uint8_t* op = out + (bh * S) * D + cg * 8;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int row = blk * kBlockRows + rl + r * RL;
+    if (row < S) {
+      float y[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = clamp448(__fdiv_rn(v[r][i], MODE == kV ? c8[i] : s));  // :72, :114, :167
+      *reinterpret_cast<uint2*>(op + (long long)row * D) = pack8_e4m3(y);
+    }
+  }
+}
+
+// Per-row absmax quantisation (fp8_linear.py:8-24): one CTA per row.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) rows_quant_kernel(const T* __restrict__ x, long long xs, int K,
+                                                              uint8_t* __restrict__ x8, float* __restrict__ scale) {
+  __shared__ float red[kThreads / 32];
+  const long long row = blockIdx.x;
+  const T* xp = x + row * xs;
+  float amax = 0.0f;
+  for (int c = threadIdx.x * 8; c < K; c += kThreads * 8) {
+    float v[8];
+    load8(xp + c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  }
+  const float s = fmaxf(block_max(amax, red), 1.0e-12f) / 448.0f;   // :20-21
+  if (threadIdx.x == 0) scale[row] = s;
+  uint8_t* op = x8 + row * K;
+  for (int c = threadIdx.x * 8; c < K; c += kThreads * 8) {
+    float v[8], y[8];
+    load8(xp + c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = clamp448(__fdiv_rn(v[i], s));   // :22
+    *reinterpret_cast<uint2*>(op + c) = pack8_e4m3(y);
+  }
+}
+
+template <typename T, int D>
+static cudaError_t run_qkv(const mh3_qkv_quant_args* a, cudaStream_t st) {
+  const int B = a->batch, H = a->heads, Sq = a->seqlen_q, Sk = a->seqlen_k;
+  const int nchunk = (Sk + kStatRows - 1) / kStatRows;
+  float* part_sum = static_cast<float*>(a->workspace);
+  float* part_amax = part_sum + (long long)B * H * nchunk * D;
+  kv_stats_kernel<T, D><<<dim3(nchunk, H, B), kThreads, 0, st>>>(
+      static_cast<const T*>(a->k), a->k_stride_b, a->k_stride_h, a->k_stride_s, static_cast<const T*>(a->v),
+      a->v_stride_b, a->v_stride_h, a->v_stride_s, Sk, H, part_sum, part_amax);
+  kv_finalize_kernel<D><<<B * H, D, 0, st>>>(part_sum, part_amax, nchunk, Sk, a->k_mean, a->scale_v);
+  const int nq = (Sq + kBlockRows - 1) / kBlockRows;
+  const int nk = (Sk + kBlockRows - 1) / kBlockRows;
+  block_quant_kernel<T, D, kQ><<<dim3(nq, H, B), kThreads, 0, st>>>(
+      static_cast<const T*>(a->q), a->q_stride_b, a->q_stride_h, a->q_stride_s, Sq, H, a->q_premul, nullptr,
+      static_cast<uint8_t*>(a->q8), a->scale_q);
+  block_quant_kernel<T, D, kK><<<dim3(nk, H, B), kThreads, 0, st>>>(
+      static_cast<const T*>(a->k), a->k_stride_b, a->k_stride_h, a->k_stride_s, Sk, H, 1.0f, a->k_mean,
+      static_cast<uint8_t*>(a->k8), a->scale_k);
+  block_quant_kernel<T, D, kV><<<dim3(nk, H, B), kThreads, 0, st>>>(
+      static_cast<const T*>(a->v), a->v_stride_b, a->v_stride_h, a->v_stride_s, Sk, H, 1.0f, a->scale_v,
+      static_cast<uint8_t*>(a->v8), nullptr);
+  return cudaGetLastError();
+}
+
+}  // namespace quant
+}  // namespace mh3
+
+using namespace mh3;
+
+extern "C" uint64_t mh3_qkv_workspace_bytes(int32_t batch, int32_t heads, int32_t seqlen_k, int32_t head_dim) {
+  if (batch <= 0 || heads <= 0 || seqlen_k <= 0 || head_dim <= 0) return 0;
+  const uint64_t nchunk = ((uint64_t)seqlen_k + quant::kStatRows - 1) / quant::kStatRows;
+  return 2ull * (uint64_t)batch * (uint64_t)heads * nchunk * (uint64_t)head_dim * sizeof(float);
+}
+
+extern "C" int mh3_quantize_qkv(const mh3_qkv_quant_args* a, void* stream) {
+  if (a == nullptr) return fail(MH3_ERR_INVALID, "mh3_quantize_qkv: null args");
+  if (a->head_dim != 64 && a->head_dim != 128) return fail(MH3_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (a->batch <= 0 || a->heads <= 0 || a->seqlen_q <= 0 || a->seqlen_k <= 0)
+    return fail(MH3_ERR_INVALID, "sizes must be positive");
+  if (a->batch > 65535 || a->heads > 65535) return fail(MH3_ERR_INVALID, "too many batches or heads");
+  if (!a->q || !a->k || !a->v || !a->q8 || !a->k8 || !a->v8 || !a->scale_q || !a->scale_k || !a->scale_v ||
+      !a->k_mean || !a->workspace)
+    return fail(MH3_ERR_INVALID, "null pointer");
+  if (a->in_dtype != MH3_DTYPE_BF16 && a->in_dtype != MH3_DTYPE_F16)
+    return fail(MH3_ERR_INVALID, "in_dtype must be bf16 or f16");
+  auto al16 = [](const void* p) { return ((uintptr_t)p & 15u) == 0; };
+  if (!al16(a->q) || !al16(a->k) || !al16(a->v) || !al16(a->q8) || !al16(a->k8) || !al16(a->v8))
+    return fail(MH3_ERR_INVALID, "tensors must be 16-byte aligned");
+  const long long st[9] = {a->q_stride_b, a->q_stride_h, a->q_stride_s, a->k_stride_b, a->k_stride_h,
+                           a->k_stride_s, a->v_stride_b, a->v_stride_h, a->v_stride_s};
+  for (long long s : st)
+    if (s % 8) return fail(MH3_ERR_INVALID, "q/k/v strides must be multiples of 8 elements");
+  cudaStream_t stream_ = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  const bool f16 = a->in_dtype == MH3_DTYPE_F16;
+  if (a->head_dim == 128)
+    e = f16 ? quant::run_qkv<__half, 128>(a, stream_) : quant::run_qkv<__nv_bfloat16, 128>(a, stream_);
+  else
+    e = f16 ? quant::run_qkv<__half, 64>(a, stream_) : quant::run_qkv<__nv_bfloat16, 64>(a, stream_);
+  if (e != cudaSuccess) return fail_cuda(e, "mh3_quantize_qkv launch");
+  return MH3_OK;
+}
+
+extern "C" int mh3_quantize_rows(const void* x, int64_t x_stride, int32_t in_dtype, int64_t M, int64_t K, void* x8,
+                                 float* scale, void* stream) {
+  if (M < 0 || K < 0) return fail(MH3_ERR_INVALID, "negative size");
+  if (M == 0 || K == 0) return MH3_OK;
+  if (!x || !x8 || !scale) return fail(MH3_ERR_INVALID, "null pointer");
+  if (K % 8 || x_stride % 8 || ((uintptr_t)x & 15u) || ((uintptr_t)x8 & 7u))
+    return fail(MH3_ERR_UNSUPPORTED, "K and the row stride must be multiples of 8, x 16-byte aligned");
+  if (M > 0x7fffffffLL) return fail(MH3_ERR_TOO_LARGE, "M too large");
+  if (in_dtype != MH3_DTYPE_BF16 && in_dtype != MH3_DTYPE_F16)
+    return fail(MH3_ERR_INVALID, "in_dtype must be bf16 or f16");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (in_dtype == MH3_DTYPE_F16)
+    quant::rows_quant_kernel<__half><<<(unsigned)M, quant::kThreads, 0, st>>>(
+        static_cast<const __half*>(x), x_stride, (int)K, static_cast<uint8_t*>(x8), scale);
+  else
+    quant::rows_quant_kernel<__nv_bfloat16><<<(unsigned)M, quant::kThreads, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), x_stride, (int)K, static_cast<uint8_t*>(x8), scale);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail_cuda(e, "mh3_quantize_rows launch");
+  return MH3_OK;
+}

@@ -1,0 +1,111 @@
+"""Drop-in replacement for the reference's ``kernels/fp8_attention.py``.
+
+Same public surface as viragadel6/minimaxh3 ``kernels/fp8_attention.py``:
+``LOG2E`` (:9), ``is_supported(q, k, v)`` (:12-36) and
+``fp8_attention(q, k, v, scale=None, key_mask=None, key_bias=None,
+repair_tau=-1.0)`` (:300-403).  The work runs in libmh3_b200 (sm_100a):
+
+1. ``mh3_quantize_qkv`` - Q scaled by softmax_scale*log2(e) and quantised
+   per 128-row block, K centred on its channel mean and quantised per
+   128-key block, V quantised per channel (the reference's granularity,
+   :39-170, :338), V kept in [key, channel] order;
+2. ``mh3_fp8_attention_fwd`` - tcgen05 FP8 flash attention with exact exp2
+   softmax (see minimaxh3_b200/csrc/attn_fwd.cu).
+
+``repair_tau`` is accepted for signature compatibility.  The reference's
+repair pass (:288-292) corrects its piecewise-linear P toward the exact
+exponential; this kernel already computes P from the exact exponential
+(rounded once to e4m3), so the argument does not change the result.
+
+The op is registered as ``torch.ops.mh3.fp8_attention`` with a fake
+(meta) implementation, so ``torch.compile``d blocks trace through it
+without a graph break.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import ops as _ops
+
+LOG2E = 1.4426950408889634
+
+
+def _device_is_sm100(device: torch.device) -> bool:
+    return torch.cuda.get_device_capability(device) == (10, 0)
+
+
+def is_supported(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> bool:
+    """Whether ``fp8_attention`` accepts these inputs (fp8_attention.py:12-36).
+
+    Same conditions as the reference: CUDA tensors on one device, 4-D,
+    bf16/fp16 of one dtype, head dim 64 or 128 on all three, equal batch and
+    head counts, Sk == Sv > 0 and Sq > 0.  The device test is sm_100 (the
+    library is built for sm_100a only) where the reference asks cc >= 8.9.
+    """
+    if not (isinstance(q, torch.Tensor) and isinstance(k, torch.Tensor) and isinstance(v, torch.Tensor)):
+        return False
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
+        return False
+    if q.device != k.device or q.device != v.device:
+        return False
+    if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
+        return False
+    if q.dtype not in (torch.bfloat16, torch.float16):
+        return False
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        return False
+    d = q.shape[-1]
+    if d not in (64, 128) or k.shape[-1] != d or v.shape[-1] != d:
+        return False
+    if q.shape[:2] != k.shape[:2] or q.shape[:2] != v.shape[:2]:
+        return False
+    if k.shape[2] != v.shape[2] or q.shape[2] == 0 or k.shape[2] == 0:
+        return False
+    return _device_is_sm100(q.device)
+
+
+def _fp8_attention_impl(q, k, v, scale, key_mask, key_bias, repair_tau):
+    B, H, Sq, D = q.shape
+    Sk = k.shape[2]
+    c = (scale if scale is not None else 1.0 / math.sqrt(D)) * LOG2E
+    q8, k8, v8, sq, sk, sv, _ = _ops.quantize_qkv(q, k, v, c)
+    bias2 = None
+    if key_mask is not None or key_bias is not None:
+        bias2 = _ops.build_key_bias2(key_mask, key_bias, B, Sk, q.device)
+    # Same strides as the reference's ``torch.empty_like(q)`` (:379); the
+    # kernel writes through the strides, so transposed views stay correct.
+    out = torch.empty_like(q)
+    if out.stride(-1) != 1 or any(s % 8 for s in out.stride()[:3]):
+        out = torch.empty((B, H, Sq, D), dtype=q.dtype, device=q.device)
+    return _ops.attention_e4m3(q8, k8, v8, sq, sk, sv, logit_scale_log2=1.0, out_dtype=q.dtype,
+                               key_bias2=bias2, out=out)
+
+
+@torch.library.custom_op("mh3::fp8_attention", mutates_args=())
+def _fp8_attention_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
+                      key_mask: torch.Tensor | None, key_bias: torch.Tensor | None,
+                      repair_tau: float) -> torch.Tensor:
+    return _fp8_attention_impl(q, k, v, None if math.isnan(scale) else scale, key_mask, key_bias, repair_tau)
+
+
+@_fp8_attention_op.register_fake
+def _(q, k, v, scale, key_mask, key_bias, repair_tau):
+    return torch.empty_like(q)
+
+
+def fp8_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    scale: float | None = None,
+    key_mask: torch.Tensor | None = None,
+    key_bias: torch.Tensor | None = None,
+    repair_tau: float = -1.0,
+) -> torch.Tensor:
+    """Non-causal FP8 attention, output in q's dtype and shape [B,H,Sq,D]."""
+    if not is_supported(q, k, v):
+        raise ValueError("Unsupported inputs for fp8_attention")
+    return torch.ops.mh3.fp8_attention(q, k, v, math.nan if scale is None else float(scale),
+                                       key_mask, key_bias, float(repair_tau))

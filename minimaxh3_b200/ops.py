@@ -1,0 +1,281 @@
+"""torch-facing wrappers over the C ABI (include/mh3_b200.h).
+
+Tensors are passed to the library as raw device pointers plus element
+strides; outputs are allocated here with torch's caching allocator on the
+current stream, as the reference's wrappers do (kernels/fp8_attention.py:
+321-379, kernels/fp8_linear.py:34-35).  No host synchronisation happens on
+these paths.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+LOG2E = 1.4426950408889634
+BLOCK = 128
+E4M3 = torch.float8_e4m3fn
+
+
+def _cdiv(a: int, b: int) -> int:
+    return (a + b - 1) // b
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.bfloat16:
+        return _lib.MH3_DTYPE_BF16
+    if dt == torch.float16:
+        return _lib.MH3_DTYPE_F16
+    raise ValueError(f"unsupported dtype {dt} (bf16 or fp16)")
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("expected CUDA tensors")
+
+
+def _scale_strides(s: torch.Tensor, nblk_full: int):
+    """Strides (b, h, blk) of a [B,H,nblk] or [B,H,1] / [B,H] scale tensor."""
+    if s.dtype != torch.float32:
+        raise ValueError("scales must be float32")
+    if s.dim() == 2:
+        return s.stride(0), s.stride(1), 0
+    if s.dim() != 3:
+        raise ValueError("scale tensors must be [B,H] or [B,H,n]")
+    if s.shape[2] == 1:
+        return s.stride(0), s.stride(1), 0
+    if s.shape[2] < nblk_full:
+        raise ValueError(f"scale has {s.shape[2]} blocks, need {nblk_full}")
+    return s.stride(0), s.stride(1), s.stride(2)
+
+
+def device_error_word(device=None) -> torch.Tensor:
+    """The library's device error word for ``device`` as a 1-element int32 view."""
+    lib = _lib.load()
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        addr = lib.mh3_device_error_word()
+    if not addr:
+        raise _lib.Mh3Error("could not resolve the device error word")
+    return _wrap_device_int(addr, dev)
+
+
+def _wrap_device_int(addr: int, dev: torch.device) -> torch.Tensor:
+    # A zero-copy int32 view of library-owned device memory.
+    class _Holder:
+        __cuda_array_interface__ = {"shape": (1,), "typestr": "<i4", "data": (addr, False), "version": 3}
+
+    with torch.cuda.device(dev):
+        return torch.as_tensor(_Holder(), device=dev)
+
+
+def read_and_clear_device_error(device=None) -> int:
+    """Synchronise ``device``, return its error word and reset it to 0 (testing/debug)."""
+    w = device_error_word(device)
+    torch.cuda.synchronize(w.device)
+    val = int(w.item())
+    w.zero_()
+    return val
+
+
+# ---------------------------------------------------------------------------
+# attention
+# ---------------------------------------------------------------------------
+
+
+def attention_e4m3(
+    q8: torch.Tensor,
+    k8: torch.Tensor,
+    v8: torch.Tensor,
+    scale_q: torch.Tensor,
+    scale_k: torch.Tensor,
+    scale_v: torch.Tensor,
+    logit_scale_log2: float = 1.0,
+    out_dtype: torch.dtype = torch.bfloat16,
+    key_bias2: torch.Tensor | None = None,
+    cu_seqlens_q: torch.Tensor | None = None,
+    cu_seqlens_k: torch.Tensor | None = None,
+    max_seqlen_q: int = 0,
+    out: torch.Tensor | None = None,
+    err: torch.Tensor | None = None,
+    timeout_ns: int = 0,
+) -> torch.Tensor:
+    """Non-causal FP8 attention (``mh3_fp8_attention_fwd``).
+
+    Dense: q8 [B,H,Sq,D], k8/v8 [B,H,Sk,D] e4m3 (channels contiguous, any
+    other strides that are multiples of 16).  Varlen (``cu_seqlens_*`` int32
+    [nseq+1] on the device): q8 [Tq,H,D], k8/v8 [Tk,H,D].  scale_q/scale_k
+    [B,H,nblk] per 128-row block, or [B,H,1] / [B,H] per (batch, head);
+    scale_v [B,H,D] or [B,H,1].  ``logit_scale_log2`` multiplies q.k (log2
+    units: softmax_scale * log2(e) when the scales do not already carry it).
+    ``key_bias2`` [B, ceil(Sk/128)*128] f32 additive log2 bias (-inf = masked,
+    and for the padding).
+    """
+    lib = _lib.load()
+    _require_cuda(q8, k8, v8, scale_q, scale_k, scale_v, key_bias2)
+    for t in (q8, k8, v8):
+        if t.dtype != E4M3:
+            raise ValueError("q8/k8/v8 must be float8_e4m3fn")
+        if t.stride(-1) != 1:
+            raise ValueError("q8/k8/v8 need a contiguous last dimension")
+    varlen = cu_seqlens_q is not None or cu_seqlens_k is not None
+    a = _lib.AttnArgs()
+    if varlen:
+        if cu_seqlens_q is None or cu_seqlens_k is None:
+            raise ValueError("varlen needs cu_seqlens_q and cu_seqlens_k")
+        if q8.dim() != 3 or k8.dim() != 3 or v8.dim() != 3:
+            raise ValueError("varlen q8/k8/v8 are [tokens, H, D]")
+        if cu_seqlens_q.dtype != torch.int32 or cu_seqlens_k.dtype != torch.int32:
+            raise ValueError("cu_seqlens must be int32")
+        Tq, H, D = q8.shape
+        Tk = k8.shape[0]
+        B = cu_seqlens_q.numel() - 1
+        if max_seqlen_q <= 0:
+            raise ValueError("varlen needs max_seqlen_q")
+        Sq, Sk = int(max_seqlen_q), 0
+        a.q_stride_b, a.q_stride_h, a.q_stride_s = 0, q8.stride(1), q8.stride(0)
+        a.k_stride_b, a.k_stride_h, a.k_stride_s = 0, k8.stride(1), k8.stride(0)
+        a.v_stride_b, a.v_stride_h, a.v_stride_s = 0, v8.stride(1), v8.stride(0)
+        a.total_q, a.total_k = Tq, Tk
+        a.cu_seqlens_q = cu_seqlens_q.data_ptr()
+        a.cu_seqlens_k = cu_seqlens_k.data_ptr()
+        a.max_seqlen_q = int(max_seqlen_q)
+        if out is None:
+            out = torch.empty((Tq, H, D), dtype=out_dtype, device=q8.device)
+        a.o_stride_b, a.o_stride_h, a.o_stride_s = 0, out.stride(1), out.stride(0)
+        nq_full = nk_full = 1
+    else:
+        if q8.dim() != 4 or k8.dim() != 4 or v8.dim() != 4:
+            raise ValueError("q8/k8/v8 are [B,H,S,D]")
+        B, H, Sq, D = q8.shape
+        Sk = k8.shape[2]
+        if k8.shape[:2] != (B, H) or v8.shape[:3] != k8.shape[:3] or k8.shape[3] != D or v8.shape[3] != D:
+            raise ValueError("q8/k8/v8 shapes disagree")
+        a.q_stride_b, a.q_stride_h, a.q_stride_s = q8.stride(0), q8.stride(1), q8.stride(2)
+        a.k_stride_b, a.k_stride_h, a.k_stride_s = k8.stride(0), k8.stride(1), k8.stride(2)
+        a.v_stride_b, a.v_stride_h, a.v_stride_s = v8.stride(0), v8.stride(1), v8.stride(2)
+        if out is None:
+            out = torch.empty((B, H, Sq, D), dtype=out_dtype, device=q8.device)
+        a.o_stride_b, a.o_stride_h, a.o_stride_s = out.stride(0), out.stride(1), out.stride(2)
+        nq_full, nk_full = _cdiv(Sq, BLOCK), _cdiv(Sk, BLOCK)
+    if out.stride(-1) != 1 or out.dtype != out_dtype:
+        raise ValueError("out must have a contiguous last dim and dtype out_dtype")
+    a.batch, a.heads, a.seqlen_q, a.seqlen_k, a.head_dim = B, H, Sq, Sk, D
+    a.out_dtype = _dtype_code(out_dtype)
+    a.q8, a.k8, a.v8, a.out = q8.data_ptr(), k8.data_ptr(), v8.data_ptr(), out.data_ptr()
+    a.scale_q = scale_q.data_ptr()
+    a.sq_stride_b, a.sq_stride_h, a.sq_stride_blk = _scale_strides(scale_q, nq_full if not varlen else 1)
+    a.scale_k = scale_k.data_ptr()
+    a.sk_stride_b, a.sk_stride_h, a.sk_stride_blk = _scale_strides(scale_k, nk_full if not varlen else 1)
+    if scale_v.dtype != torch.float32 or scale_v.dim() != 3:
+        raise ValueError("scale_v must be float32 [B,H,D] or [B,H,1]")
+    a.scale_v = scale_v.data_ptr()
+    a.sv_stride_b, a.sv_stride_h = scale_v.stride(0), scale_v.stride(1)
+    a.sv_stride_d = scale_v.stride(2) if scale_v.shape[2] != 1 else 0
+    a.logit_scale_log2 = float(logit_scale_log2)
+    if key_bias2 is not None:
+        if key_bias2.dtype != torch.float32 or key_bias2.dim() != 2 or key_bias2.stride(1) != 1:
+            raise ValueError("key_bias2 must be float32 [B, n*128] with contiguous rows")
+        a.key_bias2 = key_bias2.data_ptr()
+        a.key_bias2_stride_b = key_bias2.stride(0)
+    if err is not None:
+        a.err = err.data_ptr()
+    a.timeout_ns = int(timeout_ns)
+    with torch.cuda.device(q8.device):
+        rc = lib.mh3_fp8_attention_fwd(a, _stream(q8.device))
+    _lib.check(rc, "mh3_fp8_attention_fwd")
+    return out
+
+
+def build_key_bias2(key_mask, key_bias, B: int, Sk: int, device) -> torch.Tensor:
+    """Per-key additive bias in log2 units, [B, ceil(Sk/128)*128], -inf = masked.
+
+    Folds the reference's two per-key inputs (fp8_attention.py:256-264):
+    ``key_bias`` adds ``bias * log2(e)`` and a bias <= -1e8 masks the key;
+    ``key_mask`` False masks the key.  The padding past Sk is masked too.
+    """
+    nk = _cdiv(Sk, BLOCK)
+    buf = torch.full((B, nk * BLOCK), -math.inf, dtype=torch.float32, device=device)
+    val = torch.zeros((B, Sk), dtype=torch.float32, device=device)
+    valid = torch.ones((B, Sk), dtype=torch.bool, device=device)
+    if key_bias is not None:
+        kb = key_bias.to(device=device, dtype=torch.float32).expand(B, Sk)
+        valid = valid & (kb > -1.0e8)
+        val = kb * torch.tensor(LOG2E, dtype=torch.float32, device=device)
+    if key_mask is not None:
+        valid = valid & key_mask.to(device=device, dtype=torch.bool).expand(B, Sk)
+    buf[:, :Sk] = torch.where(valid, val, torch.full_like(val, -math.inf))
+    return buf
+
+
+# ---------------------------------------------------------------------------
+# quantisation
+# ---------------------------------------------------------------------------
+
+
+def quantize_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_premul: float):
+    """Q/K/V e4m3 quantisation of the drop-in path (``mh3_quantize_qkv``).
+
+    Returns (q8, k8, v8, scale_q, scale_k, scale_v, k_mean): q8 [B,H,Sq,D],
+    k8/v8 [B,H,Sk,D] contiguous e4m3; scale_q [B,H,ceil(Sq/128)],
+    scale_k [B,H,ceil(Sk/128)], scale_v / k_mean [B,H,D] float32.
+    """
+    lib = _lib.load()
+    _require_cuda(q, k, v)
+    B, H, Sq, D = q.shape
+    Sk = k.shape[2]
+    dev = q.device
+    tensors = []
+    for t in (q, k, v):
+        if t.stride(-1) != 1 or any(s % 8 for s in t.stride()[:3]) or t.data_ptr() % 16:
+            t = t.contiguous()
+        tensors.append(t)
+    q, k, v = tensors
+    q8 = torch.empty((B, H, Sq, D), dtype=E4M3, device=dev)
+    k8 = torch.empty((B, H, Sk, D), dtype=E4M3, device=dev)
+    v8 = torch.empty((B, H, Sk, D), dtype=E4M3, device=dev)
+    sq = torch.empty((B, H, _cdiv(Sq, BLOCK)), dtype=torch.float32, device=dev)
+    sk = torch.empty((B, H, _cdiv(Sk, BLOCK)), dtype=torch.float32, device=dev)
+    sv = torch.empty((B, H, D), dtype=torch.float32, device=dev)
+    kmean = torch.empty((B, H, D), dtype=torch.float32, device=dev)
+    ws_bytes = int(lib.mh3_qkv_workspace_bytes(B, H, Sk, D))
+    ws = torch.empty((max(ws_bytes, 16),), dtype=torch.uint8, device=dev)
+    a = _lib.QkvQuantArgs()
+    a.batch, a.heads, a.seqlen_q, a.seqlen_k, a.head_dim = B, H, Sq, Sk, D
+    a.in_dtype = _dtype_code(q.dtype)
+    a.q, a.q_stride_b, a.q_stride_h, a.q_stride_s = q.data_ptr(), q.stride(0), q.stride(1), q.stride(2)
+    a.k, a.k_stride_b, a.k_stride_h, a.k_stride_s = k.data_ptr(), k.stride(0), k.stride(1), k.stride(2)
+    a.v, a.v_stride_b, a.v_stride_h, a.v_stride_s = v.data_ptr(), v.stride(0), v.stride(1), v.stride(2)
+    a.q_premul = float(q_premul)
+    a.q8, a.k8, a.v8 = q8.data_ptr(), k8.data_ptr(), v8.data_ptr()
+    a.scale_q, a.scale_k, a.scale_v, a.k_mean = sq.data_ptr(), sk.data_ptr(), sv.data_ptr(), kmean.data_ptr()
+    a.workspace = ws.data_ptr()
+    with torch.cuda.device(dev):
+        rc = lib.mh3_quantize_qkv(a, _stream(dev))
+    _lib.check(rc, "mh3_quantize_qkv")
+    return q8, k8, v8, sq, sk, sv, kmean
+
+
+def quantize_rows(x2d: torch.Tensor):
+    """Per-row e4m3 quantisation (``mh3_quantize_rows``): (x8 [M,K], scale [M,1])."""
+    lib = _lib.load()
+    if x2d.dim() != 2 or not x2d.is_cuda:
+        raise ValueError("quantize_rows expects a 2D CUDA tensor")
+    if x2d.stride(1) != 1 or x2d.stride(0) % 8 or x2d.data_ptr() % 16:
+        x2d = x2d.contiguous()
+    M, K = x2d.shape
+    x8 = torch.empty((M, K), dtype=E4M3, device=x2d.device)
+    scale = torch.empty((M, 1), dtype=torch.float32, device=x2d.device)
+    if M > 0 and K > 0:
+        with torch.cuda.device(x2d.device):
+            rc = lib.mh3_quantize_rows(x2d.data_ptr(), x2d.stride(0), _dtype_code(x2d.dtype), M, K,
+                                       x8.data_ptr(), scale.data_ptr(), _stream(x2d.device))
+        _lib.check(rc, "mh3_quantize_rows")
+    return x8, scale
