@@ -4,8 +4,10 @@
 
 Default arm (``--impl mh3``), N=1: BASELINE config 2 - FP8 self-attention
 forward, B=1 H=40 S=32760 D=128, e4m3 q/k/v with per-(batch, head) scales
-(synthetic N(0,1) with one of 128 channels x8, seed 0), bf16 out.  A step is
-one ``mh3_fp8_attention_fwd`` launch; ``value`` is whole-job TFLOP/s
+(synthetic N(0,1) with one of 128 channels x8, seed 0), bf16 out.  With the
+default 16-bit PV product (``--pv f16``) a step is one exact e4m3->f16
+widening of V plus one ``mh3_fp8_attention_fwd`` launch; with ``--pv e4m3``
+it is the attention launch alone.  ``value`` is whole-job TFLOP/s
 (4*B*H*S^2*D per step) with inputs resident in HBM (504 MB of e4m3 inputs,
 larger than the 126 MB L2).  ``e2e`` times the drop-in
 ``kernels.fp8_attention.fp8_attention`` on bf16 tensors copied from pinned
@@ -38,7 +40,6 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 B, H, S, D = 1, 40, 32760, 128
-FLOP_PER_CALL = 4.0 * B * H * S * S * D
 NOMINAL_FP8_TFLOPS = 4500.0
 
 
@@ -196,6 +197,9 @@ def run_reference_arm(args, rank):
 
 
 def run_gpu_arm(args, dist, rank, world, local):
+    global H
+    H = args.heads
+    FLOP_PER_CALL = 4.0 * B * H * S * S * D
     from minimaxh3_b200 import ops
     from minimaxh3_b200.kernels.fp8_attention import fp8_attention
 
@@ -206,9 +210,21 @@ def run_gpu_arm(args, dist, rank, world, local):
     ls2 = 1.4426950408889634 / math.sqrt(D)
     out = torch.empty(B, H, S, D, dtype=torch.bfloat16, device=dev)
     stream = torch.cuda.current_stream(dev)
+    v16 = torch.empty(B, H, S, D, dtype=torch.float16, device=dev)
+    lib = ops._lib.load()
+    attn_ev = []
 
-    def step():
-        ops.attention_e4m3(q8, k8, v8, sq, sk, sv, logit_scale_log2=ls2, out=out)
+    def step(record=None):
+        vin = v8
+        if args.pv == "f16":
+            rc = lib.mh3_widen_e4m3_to_f16(v8.data_ptr(), v16.data_ptr(), v8.numel(), stream.cuda_stream)
+            ops._lib.check(rc, "widen")
+            vin = v16
+        if record is not None:
+            record[0].record(stream)
+        ops.attention_e4m3(q8, k8, vin, sq, sk, sv, logit_scale_log2=ls2, out=out)
+        if record is not None:
+            record[1].record(stream)
 
     for _ in range(args.warmup):
         step()
@@ -223,9 +239,7 @@ def run_gpu_arm(args, dist, rank, world, local):
         t_end = torch.cuda.Event(enable_timing=True)
         t_start.record(stream)
         for i in range(args.steps):
-            starts[i].record(stream)
-            step()
-            ends[i].record(stream)
+            step((starts[i], ends[i]))
         t_end.record(stream)
         torch.cuda.synchronize(dev)
     if dist:
@@ -241,6 +255,10 @@ def run_gpu_arm(args, dist, rank, world, local):
     avg_launch_ms = sum(per_launch) / len(per_launch)
     achieved = FLOP_PER_CALL / (avg_launch_ms / 1e3) / 1e12
     peaks = _peaks()
+    if args.no_extras:
+        if rank == 0:
+            print(json.dumps({"value": value, "avg_launch_ms": avg_launch_ms, "achieved": achieved, "heads": H}))
+        return
 
     # End to end through the drop-in API: pinned host bf16 in, bf16 out back to host.
     e2e_steps = max(1, min(args.steps, 3))
@@ -290,10 +308,10 @@ def run_gpu_arm(args, dist, rank, world, local):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "e4m3",
+        "dtype": "e4m3 QK^T, " + ("f16 PV" if args.pv == "f16" else "e4m3 PV"),
         "data": "synthetic",
         "config": {"workload": "config2: FP8 self-attention fwd B=1 H=40 S=32760 D=128, per-(b,h) scales, "
-                               "bf16 out", "inputs_vs_l2": "inputs 504 MB > 126 MB L2 (no flush)",
+                               "bf16 out", "pv": args.pv, "inputs_vs_l2": "inputs 504 MB > 126 MB L2 (no flush)",
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
         "pct_of_fp8_peak": achieved / peaks["fp8_tflops"],
         "pct_of_nominal_fp8_peak": achieved / NOMINAL_FP8_TFLOPS,
@@ -303,7 +321,7 @@ def run_gpu_arm(args, dist, rank, world, local):
         "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "minimaxh3_b200.kernels.fp8_attention.fp8_attention (bf16 in/out, quantise + attention)",
                 "steps": e2e_steps},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * (2 if args.pv == "f16" else 1),
         "clocks": clk.summary(),
     }
     if cpu is not None:
@@ -318,6 +336,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="mh3", choices=["mh3", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--heads", type=int, default=40, help="heads (40 = config 2; fewer for ncu captures)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="kernel timing only (no e2e, no CPU baseline): the ncu capture command")
+    ap.add_argument("--pv", default="f16", choices=["f16", "e4m3"],
+                    help="PV product operands: f16 P/V (default, meets the tolerance) or e4m3")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "mh3":
         args.warmup = 3

@@ -42,6 +42,7 @@ extern "C" {
 
 #define MH3_DTYPE_BF16 0
 #define MH3_DTYPE_F16 1
+#define MH3_DTYPE_E4M3 2
 
 /* Device-side error codes written by kernels into an ``err`` word. */
 #define MH3_DEVERR_NONE 0
@@ -71,6 +72,10 @@ MH3_API int* mh3_device_error_word(void);
  * blk(i) = i / 128 within the sequence.  A per-(batch, head) scale is a
  * block stride of 0.  Rows whose keys are all masked produce 0.
  *
+ * v_dtype selects the PV product: MH3_DTYPE_E4M3 (P rounded to e4m3, e4m3 V,
+ * kind::f8f6f4) or MH3_DTYPE_F16 (P in f16, V an f16 tensor already divided
+ * by scale_v, kind::f16 - the accurate default of the drop-in path).
+ *
  * Dense mode (cu_seqlens_q == cu_seqlens_k == NULL): q8 is [B,H,Sq,D],
  * k8/v8 are [B,H,Sk,D] under the given strides.
  * Varlen mode: tensors are packed along the token dimension (the ``s``
@@ -85,8 +90,10 @@ MH3_API int* mh3_device_error_word(void);
 typedef struct mh3_attn_args {
   int32_t batch, heads, seqlen_q, seqlen_k, head_dim; /* head_dim: 64 or 128 */
   int32_t out_dtype;                                   /* MH3_DTYPE_BF16 / MH3_DTYPE_F16 */
+  int32_t v_dtype;                                     /* MH3_DTYPE_E4M3 / MH3_DTYPE_F16 */
+  int32_t reserved0;
   const void* q8;
-  int64_t q_stride_b, q_stride_h, q_stride_s; /* multiples of 16 */
+  int64_t q_stride_b, q_stride_h, q_stride_s; /* multiples of 16 (v: of 16 bytes) */
   const void* k8;
   int64_t k_stride_b, k_stride_h, k_stride_s;
   const void* v8;
@@ -123,6 +130,8 @@ MH3_API int mh3_fp8_attention_fwd(const mh3_attn_args* args, void* stream);
  *   q8 = e4m3(clamp(q*q_premul / sq, +-448)), sq = max(absmax_128rows, 1e-12)/448
  *   k8 = e4m3(clamp((k-mean_k)/sk, +-448)),    sk per 128 keys likewise
  *   v8 = e4m3(clamp(v / sv[d], +-448)),        sv[d] = max(absmax over S, 1e-12)/448
+ * (v_out_dtype = MH3_DTYPE_F16 stores f16(v / sv[d]) instead of e4m3, for the
+ * attention kernel's f16 PV product.)
  * Outputs are contiguous: q8 [B,H,Sq,D], k8/v8 [B,H,Sk,D] (v8 in natural
  * [key, channel] order - the attention kernel needs no transposed copy),
  * scale_q [B,H,ceil(Sq/128)], scale_k [B,H,ceil(Sk/128)], scale_v and
@@ -137,7 +146,8 @@ typedef struct mh3_qkv_quant_args {
   int64_t k_stride_b, k_stride_h, k_stride_s;
   const void* v;
   int64_t v_stride_b, v_stride_h, v_stride_s;
-  float q_premul; /* softmax scale * log2(e) */
+  float q_premul;      /* softmax scale * log2(e) */
+  int32_t v_out_dtype; /* MH3_DTYPE_E4M3 (reference layout) or MH3_DTYPE_F16 */
   void* q8;
   void* k8;
   void* v8;
@@ -162,6 +172,14 @@ MH3_API int mh3_quantize_qkv(const mh3_qkv_quant_args* args, void* stream);
  */
 MH3_API int mh3_quantize_rows(const void* x, int64_t x_stride, int32_t in_dtype, int64_t M, int64_t K, void* x8,
                       float* scale, void* stream);
+
+/*
+ * Exact widening of e4m3 to f16 (every e4m3 value is an f16 value): dst[i] =
+ * src[i] for n contiguous elements.  Feeds pre-quantised e4m3 V to the
+ * attention kernel's f16 PV product.  No reference counterpart (the
+ * reference's PV product is e4m3 only).
+ */
+MH3_API int mh3_widen_e4m3_to_f16(const void* src, void* dst, int64_t n, void* stream);
 
 #ifdef __cplusplus
 }

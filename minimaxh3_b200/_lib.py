@@ -20,6 +20,7 @@ MH3_ERR_DRIVER = -3
 MH3_ERR_TOO_LARGE = -4
 MH3_DTYPE_BF16 = 0
 MH3_DTYPE_F16 = 1
+MH3_DTYPE_E4M3 = 2
 MH3_DEVERR_WAIT_TIMEOUT = 1
 
 c_i32 = ctypes.c_int32
@@ -34,7 +35,7 @@ class AttnArgs(ctypes.Structure):
 
     _fields_ = [
         ("batch", c_i32), ("heads", c_i32), ("seqlen_q", c_i32), ("seqlen_k", c_i32),
-        ("head_dim", c_i32), ("out_dtype", c_i32),
+        ("head_dim", c_i32), ("out_dtype", c_i32), ("v_dtype", c_i32), ("reserved0", c_i32),
         ("q8", c_ptr), ("q_stride_b", c_i64), ("q_stride_h", c_i64), ("q_stride_s", c_i64),
         ("k8", c_ptr), ("k_stride_b", c_i64), ("k_stride_h", c_i64), ("k_stride_s", c_i64),
         ("v8", c_ptr), ("v_stride_b", c_i64), ("v_stride_h", c_i64), ("v_stride_s", c_i64),
@@ -59,7 +60,7 @@ class QkvQuantArgs(ctypes.Structure):
         ("q", c_ptr), ("q_stride_b", c_i64), ("q_stride_h", c_i64), ("q_stride_s", c_i64),
         ("k", c_ptr), ("k_stride_b", c_i64), ("k_stride_h", c_i64), ("k_stride_s", c_i64),
         ("v", c_ptr), ("v_stride_b", c_i64), ("v_stride_h", c_i64), ("v_stride_s", c_i64),
-        ("q_premul", c_f32),
+        ("q_premul", c_f32), ("v_out_dtype", c_i32),
         ("q8", c_ptr), ("k8", c_ptr), ("v8", c_ptr),
         ("scale_q", c_ptr), ("scale_k", c_ptr), ("scale_v", c_ptr), ("k_mean", c_ptr),
         ("workspace", c_ptr),
@@ -75,6 +76,7 @@ _SIGNATURES = {
     "mh3_qkv_workspace_bytes": (c_u64, [c_i32, c_i32, c_i32, c_i32]),
     "mh3_quantize_qkv": (c_i32, [ctypes.POINTER(QkvQuantArgs), c_ptr]),
     "mh3_quantize_rows": (c_i32, [c_ptr, c_i64, c_i32, c_i64, c_i64, c_ptr, c_ptr, c_ptr]),
+    "mh3_widen_e4m3_to_f16": (c_i32, [c_ptr, c_ptr, c_i64, c_ptr]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

@@ -65,11 +65,11 @@ struct Params {
   unsigned long long timeout_ns;
 };
 
-template <int D>
+template <int D, bool PV16>
 struct __align__(1024) Smem {
   uint8_t q[2][BM * D];
   uint8_t k[KST][BN * D];
-  uint8_t v[VST][BN * D];
+  uint8_t v[VST][BN * D * (PV16 ? 2 : 1)];
   uint64_t bar_q;
   uint64_t bar_kfull[KST];
   uint64_t bar_kempty[KST];
@@ -82,18 +82,21 @@ struct __align__(1024) Smem {
   int abort_flag;
 };
 
-template <int D>
+template <int D, bool PV16>
 constexpr uint32_t smem_bytes() {
-  return (uint32_t)sizeof(Smem<D>) + 1024;
+  return (uint32_t)sizeof(Smem<D, PV16>) + 1024;
 }
 
 __device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
 __device__ __forceinline__ uint32_t f2u(float x) { return __float_as_uint(x); }
 
-template <int D, bool OUT_F16, bool HAS_BIAS>
+// PV16: the PV product runs on f16 operands (P = f16 straight from the packed
+// ex2, V an f16 tensor pre-scaled per channel) instead of e4m3; same flow.
+template <int D, bool OUT_F16, bool HAS_BIAS, bool PV16>
 __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
-  Smem<D>& sm = *reinterpret_cast<Smem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  using SmemT = Smem<D, PV16>;
+  SmemT& sm = *reinterpret_cast<SmemT*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int h = blockIdx.y;
@@ -115,6 +118,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
   constexpr uint32_t kLayout = (D == 128) ? kLayoutSW128 : kLayoutSW64;
   constexpr uint32_t kRowBytes = D;
   constexpr uint32_t kTileBytes = BN * D;
+  constexpr uint32_t kVTileBytes = BN * D * (PV16 ? 2 : 1);
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&sm.bar_q), 1);
@@ -168,8 +172,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
           issued = -(j + 1);  // K(j) issued, V(j) not
           break;
         }
-        mbar_arrive_expect_tx(smem_u32(&sm.bar_vfull[vs]), kTileBytes);
-        tma_load_4d(smem_u32(sm.v[vs]), &p.tmv, smem_u32(&sm.bar_vfull[vs]), 0, k_start + j * BN, h, bcoord);
+        mbar_arrive_expect_tx(smem_u32(&sm.bar_vfull[vs]), kVTileBytes);
+        if constexpr (PV16) {
+          // f16 V: 64-channel boxes (128 bytes wide), one swizzle-128B atom column each
+#pragma unroll
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_4d(smem_u32(sm.v[vs]) + c * (BN * 128), &p.tmv, smem_u32(&sm.bar_vfull[vs]), c * 64,
+                        k_start + j * BN, h, bcoord);
+        } else {
+          tma_load_4d(smem_u32(sm.v[vs]), &p.tmv, smem_u32(&sm.bar_vfull[vs]), 0, k_start + j * BN, h, bcoord);
+        }
         issued = j + 1;
       }
       // Teardown: let the last copy issued into each stage land before exit.
@@ -183,7 +195,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
     } else if (warp == 9 && lane == 0) {
       // ---------------------------------------------------------------- MMA issuer
       constexpr uint32_t kIdescS = idesc_e4m3(BM, BN, false, false);
-      constexpr uint32_t kIdescO = idesc_e4m3(BM, D, false, true);
+      constexpr uint32_t kIdescO = PV16 ? idesc_f16(BM, D, false, true) : idesc_e4m3(BM, D, false, true);
       const uint32_t tS[2] = {tmem + 0u, tmem + 128u};
       const uint32_t tO[2] = {tmem + 256u, tmem + 256u + (uint32_t)D};
       const uint32_t q_base[2] = {smem_u32(sm.q[0]), smem_u32(sm.q[1])};
@@ -192,7 +204,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
       // across D channels, 8-key groups D*8 bytes apart, 32 keys per MMA.
       auto kmaj = [&](uint32_t base, int kk) { return smem_desc(base + kk * 32, 16, 8 * kRowBytes, kLayout); };
       auto vdesc = [&](int vs, int kk) {
-        return smem_desc(smem_u32(sm.v[vs]) + kk * 32 * kRowBytes, kTileBytes, 8 * kRowBytes, kLayout);
+        if constexpr (PV16)  // 16 keys per MMA; atom columns of 64 channels, BN*128 bytes apart
+          return smem_desc(smem_u32(sm.v[vs]) + kk * 16 * 128, BN * 128, 8 * 128, kLayoutSW128);
+        else
+          return smem_desc(smem_u32(sm.v[vs]) + kk * 32 * kRowBytes, kTileBytes, 8 * kRowBytes, kLayout);
       };
       auto issue_s = [&](int t, int ks) {
         const uint32_t kb = smem_u32(sm.k[ks]);
@@ -217,9 +232,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
         for (int t = 0; t < 2; ++t) {
           mbar_wait(smem_u32(&sm.bar_p[t]), (uint32_t)j & 1u, g);
           tc_fence_after();
+          if constexpr (PV16) {
 #pragma unroll
-          for (int kk = 0; kk < BN / 32; ++kk)
-            mma_f8_ts(tO[t], tS[t] + (uint32_t)(kk * 8), vdesc(vs, kk), kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < BN / 16; ++kk)
+              mma_f16_ts(tO[t], tS[t] + (uint32_t)(kk * 8), vdesc(vs, kk), kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < BN / 32; ++kk)
+              mma_f8_ts(tO[t], tS[t] + (uint32_t)(kk * 8), vdesc(vs, kk), kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+          }
           if (t == 1) mma_commit(smem_u32(&sm.bar_vempty[vs]));
           if (j + 1 < nk) {
             if (t == 0) {
@@ -324,27 +345,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
 
       const float nb = P_OFFSET - m;
       const float2 nn = make_float2(nb, nb);
-      uint32_t pk[32];
       float lsum = 0.0f;
+      // P for 32 keys at a time: f16 pairs (PV16, 16 columns) or e4m3
+      // quads (8 columns), stored over the first columns of S.
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t hacc = 0u;
+        uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const float2 x = ffma2(make_float2(u2f(sr[c][2 * i]), u2f(sr[c][2 * i + 1])), cc, nn);
           const uint32_t e = ex2_f16x2(cvt_f16x2(x.y, x.x));
           hacc = hadd2(hacc, e);
-          const uint32_t p2 = cvt_e4m3x2_f16x2(e);
-          if (i & 1)
-            pk[c * 8 + (i >> 1)] |= p2 << 16;
-          else
-            pk[c * 8 + (i >> 1)] = p2;
+          if constexpr (PV16) {
+            pk[i] = e;
+          } else {
+            const uint32_t p2 = cvt_e4m3x2_f16x2(e);
+            if (i & 1)
+              pk[i >> 1] |= p2 << 16;
+            else
+              pk[i >> 1] = p2;
+          }
         }
         const float2 hs = f16x2_to_float2(hacc);
         lsum += hs.x + hs.y;
+        if constexpr (PV16)
+          tmem_st16(tS + (uint32_t)(c * 16), pk);
+        else
+          tmem_st8(tS + (uint32_t)(c * 8), pk);
       }
       l += lsum;
-      tmem_st32(tS, pk);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -407,29 +437,39 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
 // host side
 // ------------------------------------------------------------------------------
 
+// dims (D, S, H, B) innermost first; element strides ss/sh/sb for dims 1..3.
+// e4m3: box (D, 128) with a D-byte swizzle; f16: box (64, 128), swizzle 128B.
 static int make_map(CUtensorMap* map, const void* base, int D, long long S, int H, int B, long long ss,
-                    long long sh, long long sb) {
-  // dims (D, S, H, B) innermost first; strides in bytes for dims 1..3.
+                    long long sh, long long sb, bool f16) {
+  const long long es = f16 ? 2 : 1;
   const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
-  const cuuint64_t strides[3] = {(cuuint64_t)ss, (cuuint64_t)sh, (cuuint64_t)sb};
-  const cuuint32_t box[4] = {(cuuint32_t)D, (cuuint32_t)BN, 1u, 1u};
+  const cuuint64_t strides[3] = {(cuuint64_t)(ss * es), (cuuint64_t)(sh * es), (cuuint64_t)(sb * es)};
+  const cuuint32_t box[4] = {(cuuint32_t)(f16 ? 64 : D), (cuuint32_t)BN, 1u, 1u};
   const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
-  const CUtensorMapSwizzle sw = (D == 128) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  return encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, box, estr,
-                      sw);
+  const CUtensorMapSwizzle sw =
+      (f16 || D == 128) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  return encode_tiled(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 4,
+                      const_cast<void*>(base), dims, strides, box, estr, sw);
 }
 
-template <int D, bool F16, bool BIAS>
+template <int D, bool F16, bool BIAS, bool PV16>
 static cudaError_t launch(const Params& p, dim3 grid, cudaStream_t st) {
-  auto kern = fwd_kernel<D, F16, BIAS>;
+  auto kern = fwd_kernel<D, F16, BIAS, PV16>;
+  constexpr uint32_t bytes = smem_bytes<D, PV16>();
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes<D>());
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
   });
   if (attr_err != cudaSuccess) return attr_err;
-  kern<<<grid, NUM_THREADS, smem_bytes<D>(), st>>>(p);
+  kern<<<grid, NUM_THREADS, bytes, st>>>(p);
   return cudaGetLastError();
+}
+
+template <int D, bool PV16>
+static cudaError_t dispatch(const Params& p, dim3 grid, cudaStream_t st, bool f16, bool bias) {
+  if (f16) return bias ? launch<D, true, true, PV16>(p, grid, st) : launch<D, true, false, PV16>(p, grid, st);
+  return bias ? launch<D, false, true, PV16>(p, grid, st) : launch<D, false, false, PV16>(p, grid, st);
 }
 
 }  // namespace attn
@@ -452,6 +492,8 @@ extern "C" int mh3_fp8_attention_fwd(const mh3_attn_args* a, void* stream) {
     return fail(MH3_ERR_INVALID, "null tensor pointer");
   if (a->out_dtype != MH3_DTYPE_BF16 && a->out_dtype != MH3_DTYPE_F16)
     return fail(MH3_ERR_INVALID, "out_dtype must be bf16 or f16");
+  if (a->v_dtype != MH3_DTYPE_E4M3 && a->v_dtype != MH3_DTYPE_F16)
+    return fail(MH3_ERR_INVALID, "v_dtype must be e4m3 or f16");
   // TMA: 16-byte aligned bases and strides; output rows written as 16-byte vectors.
   auto al16 = [](const void* p_) { return ((uintptr_t)p_ & 15u) == 0; };
   if (!al16(a->q8) || !al16(a->k8) || !al16(a->v8) || !al16(a->out))
@@ -459,9 +501,10 @@ extern "C" int mh3_fp8_attention_fwd(const mh3_attn_args* a, void* stream) {
   const long long qs[3] = {a->q_stride_s, a->q_stride_h, a->q_stride_b};
   const long long ks[3] = {a->k_stride_s, a->k_stride_h, a->k_stride_b};
   const long long vs[3] = {a->v_stride_s, a->v_stride_h, a->v_stride_b};
+  const long long vmul = a->v_dtype == MH3_DTYPE_F16 ? 8 : 16;
   for (int i = 0; i < 3; ++i) {
-    if ((qs[i] % 16) || (ks[i] % 16) || (vs[i] % 16))
-      return fail(MH3_ERR_INVALID, "q8/k8/v8 strides must be multiples of 16 elements");
+    if ((qs[i] % 16) || (ks[i] % 16) || (vs[i] % vmul))
+      return fail(MH3_ERR_INVALID, "q8/k8 strides must be multiples of 16 elements, v of 16 bytes");
   }
   if ((a->o_stride_s % 8) || (a->o_stride_h % 8) || (a->o_stride_b % 8))
     return fail(MH3_ERR_INVALID, "output strides must be multiples of 8 elements");
@@ -475,14 +518,15 @@ extern "C" int mh3_fp8_attention_fwd(const mh3_attn_args* a, void* stream) {
   const long long Sk_dim = varlen ? a->total_k : a->seqlen_k;
   if (varlen && (Sq_dim <= 0 || Sk_dim <= 0)) return fail(MH3_ERR_INVALID, "varlen needs total_q/total_k > 0");
   const int Bdim = varlen ? 1 : B;
+  const bool pv16 = a->v_dtype == MH3_DTYPE_F16;
   int rc = attn::make_map(&p.tmq, a->q8, D, Sq_dim, H, Bdim, a->q_stride_s, a->q_stride_h,
-                          varlen ? Sq_dim * a->q_stride_s : a->q_stride_b);
+                          varlen ? Sq_dim * a->q_stride_s : a->q_stride_b, false);
   if (rc) return rc;
   rc = attn::make_map(&p.tmk, a->k8, D, Sk_dim, H, Bdim, a->k_stride_s, a->k_stride_h,
-                      varlen ? Sk_dim * a->k_stride_s : a->k_stride_b);
+                      varlen ? Sk_dim * a->k_stride_s : a->k_stride_b, false);
   if (rc) return rc;
   rc = attn::make_map(&p.tmv, a->v8, D, Sk_dim, H, Bdim, a->v_stride_s, a->v_stride_h,
-                      varlen ? Sk_dim * a->v_stride_s : a->v_stride_b);
+                      varlen ? Sk_dim * a->v_stride_s : a->v_stride_b, pv16);
   if (rc) return rc;
   p.out = a->out;
   p.osb = a->o_stride_b;
@@ -519,17 +563,10 @@ extern "C" int mh3_fp8_attention_fwd(const mh3_attn_args* a, void* stream) {
   const bool f16 = a->out_dtype == MH3_DTYPE_F16;
   const bool bias = a->key_bias2 != nullptr;
   cudaError_t e;
-  if (D == 128) {
-    if (f16)
-      e = bias ? attn::launch<128, true, true>(p, grid, st) : attn::launch<128, true, false>(p, grid, st);
-    else
-      e = bias ? attn::launch<128, false, true>(p, grid, st) : attn::launch<128, false, false>(p, grid, st);
-  } else {
-    if (f16)
-      e = bias ? attn::launch<64, true, true>(p, grid, st) : attn::launch<64, true, false>(p, grid, st);
-    else
-      e = bias ? attn::launch<64, false, true>(p, grid, st) : attn::launch<64, false, false>(p, grid, st);
-  }
+  if (D == 128)
+    e = pv16 ? attn::dispatch<128, true>(p, grid, st, f16, bias) : attn::dispatch<128, false>(p, grid, st, f16, bias);
+  else
+    e = pv16 ? attn::dispatch<64, true>(p, grid, st, f16, bias) : attn::dispatch<64, false>(p, grid, st, f16, bias);
   if (e != cudaSuccess) return fail_cuda(e, "mh3_fp8_attention_fwd launch");
   return MH3_OK;
 }

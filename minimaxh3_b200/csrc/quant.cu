@@ -134,7 +134,7 @@ enum Mode { kQ = 0, kK = 1, kV = 2 };
 
 // One 128-row block of one (b, h): transform, block absmax (Q, K), divide,
 // clamp, e4m3.  Output contiguous [B,H,S,D]; scale [B,H,nblk].
-template <typename T, int D, int MODE>
+template <typename T, int D, int MODE, bool OUT_F16 = false>
 __global__ void __launch_bounds__(kThreads) block_quant_kernel(const T* __restrict__ x, long long sb, long long sh,
                                                                long long ss, int S, int H, float premul,
                                                                const float* __restrict__ chan /* mean or sv */,
@@ -178,7 +178,8 @@ __global__ void __launch_bounds__(kThreads) block_quant_kernel(const T* __restri
     s = fmaxf(bm, 1.0e-12f) / 448.0f;                  // :71, :113
     if (threadIdx.x == 0) scale[bh * nblk + blk] = s;
   }
-  uint8_t* op = out + (bh * S) * D + cg * 8;
+  constexpr int ES = OUT_F16 ? 2 : 1;  // output element size
+  uint8_t* op = out + ((bh * S) * D + cg * 8) * ES;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const int row = blk * kBlockRows + rl + r * RL;
@@ -186,7 +187,16 @@ __global__ void __launch_bounds__(kThreads) block_quant_kernel(const T* __restri
       float y[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) y[i] = clamp448(__fdiv_rn(v[r][i], MODE == kV ? c8[i] : s));  // :72, :114, :167
-      *reinterpret_cast<uint2*>(op + (long long)row * D) = pack8_e4m3(y);
+      if constexpr (OUT_F16) {
+        uint4 u;
+        u.x = cvt_f16x2(y[1], y[0]);
+        u.y = cvt_f16x2(y[3], y[2]);
+        u.z = cvt_f16x2(y[5], y[4]);
+        u.w = cvt_f16x2(y[7], y[6]);
+        *reinterpret_cast<uint4*>(op + (long long)row * D * ES) = u;
+      } else {
+        *reinterpret_cast<uint2*>(op + (long long)row * D) = pack8_e4m3(y);
+      }
     }
   }
 }
@@ -235,10 +245,34 @@ static cudaError_t run_qkv(const mh3_qkv_quant_args* a, cudaStream_t st) {
   block_quant_kernel<T, D, kK><<<dim3(nk, H, B), kThreads, 0, st>>>(
       static_cast<const T*>(a->k), a->k_stride_b, a->k_stride_h, a->k_stride_s, Sk, H, 1.0f, a->k_mean,
       static_cast<uint8_t*>(a->k8), a->scale_k);
-  block_quant_kernel<T, D, kV><<<dim3(nk, H, B), kThreads, 0, st>>>(
-      static_cast<const T*>(a->v), a->v_stride_b, a->v_stride_h, a->v_stride_s, Sk, H, 1.0f, a->scale_v,
-      static_cast<uint8_t*>(a->v8), nullptr);
+  if (a->v_out_dtype == MH3_DTYPE_F16)
+    block_quant_kernel<T, D, kV, true><<<dim3(nk, H, B), kThreads, 0, st>>>(
+        static_cast<const T*>(a->v), a->v_stride_b, a->v_stride_h, a->v_stride_s, Sk, H, 1.0f, a->scale_v,
+        static_cast<uint8_t*>(a->v8), nullptr);
+  else
+    block_quant_kernel<T, D, kV><<<dim3(nk, H, B), kThreads, 0, st>>>(
+        static_cast<const T*>(a->v), a->v_stride_b, a->v_stride_h, a->v_stride_s, Sk, H, 1.0f, a->scale_v,
+        static_cast<uint8_t*>(a->v8), nullptr);
   return cudaGetLastError();
+}
+
+// e4m3 -> f16, 16 elements per thread per step (exact: e4m3 is a subset of f16).
+__global__ void widen_e4m3_f16_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, long long n16) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n16; i += (long long)gridDim.x * blockDim.x) {
+    const uint4 u = src[i];
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t lo, hi;
+      asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(lo) : "h"((uint16_t)(w[k] & 0xffffu)));
+      asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(hi) : "h"((uint16_t)(w[k] >> 16)));
+      o[2 * k] = lo;
+      o[2 * k + 1] = hi;
+    }
+    dst[2 * i] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[2 * i + 1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
 }
 
 }  // namespace quant
@@ -263,6 +297,8 @@ extern "C" int mh3_quantize_qkv(const mh3_qkv_quant_args* a, void* stream) {
     return fail(MH3_ERR_INVALID, "null pointer");
   if (a->in_dtype != MH3_DTYPE_BF16 && a->in_dtype != MH3_DTYPE_F16)
     return fail(MH3_ERR_INVALID, "in_dtype must be bf16 or f16");
+  if (a->v_out_dtype != MH3_DTYPE_E4M3 && a->v_out_dtype != MH3_DTYPE_F16)
+    return fail(MH3_ERR_INVALID, "v_out_dtype must be e4m3 or f16");
   auto al16 = [](const void* p) { return ((uintptr_t)p & 15u) == 0; };
   if (!al16(a->q) || !al16(a->k) || !al16(a->v) || !al16(a->q8) || !al16(a->k8) || !al16(a->v8))
     return fail(MH3_ERR_INVALID, "tensors must be 16-byte aligned");
@@ -300,5 +336,22 @@ extern "C" int mh3_quantize_rows(const void* x, int64_t x_stride, int32_t in_dty
         static_cast<const __nv_bfloat16*>(x), x_stride, (int)K, static_cast<uint8_t*>(x8), scale);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "mh3_quantize_rows launch");
+  return MH3_OK;
+}
+
+extern "C" int mh3_widen_e4m3_to_f16(const void* src, void* dst, int64_t n, void* stream) {
+  if (n < 0) return fail(MH3_ERR_INVALID, "negative size");
+  if (n == 0) return MH3_OK;
+  if (!src || !dst) return fail(MH3_ERR_INVALID, "null pointer");
+  if ((n % 16) || ((uintptr_t)src & 15u) || ((uintptr_t)dst & 15u))
+    return fail(MH3_ERR_UNSUPPORTED, "n must be a multiple of 16 and both buffers 16-byte aligned");
+  const long long n16 = n / 16;
+  const int threads = 256;
+  const long long want = (n16 + threads - 1) / threads;
+  const int blocks = (int)(want < 148 * 16 ? want : 148 * 16);
+  quant::widen_e4m3_f16_kernel<<<blocks, threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), static_cast<uint4*>(dst), n16);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail_cuda(e, "mh3_widen_e4m3_to_f16 launch");
   return MH3_OK;
 }

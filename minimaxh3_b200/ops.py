@@ -110,7 +110,9 @@ def attention_e4m3(
     """Non-causal FP8 attention (``mh3_fp8_attention_fwd``).
 
     Dense: q8 [B,H,Sq,D], k8/v8 [B,H,Sk,D] e4m3 (channels contiguous, any
-    other strides that are multiples of 16).  Varlen (``cu_seqlens_*`` int32
+    other strides that are multiples of 16).  ``v8`` may instead be float16
+    (V already divided by scale_v): the PV product then runs on f16 P and V
+    instead of e4m3.  Varlen (``cu_seqlens_*`` int32
     [nseq+1] on the device): q8 [Tq,H,D], k8/v8 [Tk,H,D].  scale_q/scale_k
     [B,H,nblk] per 128-row block, or [B,H,1] / [B,H] per (batch, head);
     scale_v [B,H,D] or [B,H,1].  ``logit_scale_log2`` multiplies q.k (log2
@@ -120,9 +122,12 @@ def attention_e4m3(
     """
     lib = _lib.load()
     _require_cuda(q8, k8, v8, scale_q, scale_k, scale_v, key_bias2)
-    for t in (q8, k8, v8):
+    for t in (q8, k8):
         if t.dtype != E4M3:
-            raise ValueError("q8/k8/v8 must be float8_e4m3fn")
+            raise ValueError("q8/k8 must be float8_e4m3fn")
+    if v8.dtype not in (E4M3, torch.float16):
+        raise ValueError("v8 must be float8_e4m3fn or float16")
+    for t in (q8, k8, v8):
         if t.stride(-1) != 1:
             raise ValueError("q8/k8/v8 need a contiguous last dimension")
     varlen = cu_seqlens_q is not None or cu_seqlens_k is not None
@@ -169,6 +174,7 @@ def attention_e4m3(
         raise ValueError("out must have a contiguous last dim and dtype out_dtype")
     a.batch, a.heads, a.seqlen_q, a.seqlen_k, a.head_dim = B, H, Sq, Sk, D
     a.out_dtype = _dtype_code(out_dtype)
+    a.v_dtype = _lib.MH3_DTYPE_F16 if v8.dtype == torch.float16 else _lib.MH3_DTYPE_E4M3
     a.q8, a.k8, a.v8, a.out = q8.data_ptr(), k8.data_ptr(), v8.data_ptr(), out.data_ptr()
     a.scale_q = scale_q.data_ptr()
     a.sq_stride_b, a.sq_stride_h, a.sq_stride_blk = _scale_strides(scale_q, nq_full if not varlen else 1)
@@ -220,12 +226,14 @@ def build_key_bias2(key_mask, key_bias, B: int, Sk: int, device) -> torch.Tensor
 # ---------------------------------------------------------------------------
 
 
-def quantize_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_premul: float):
+def quantize_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_premul: float,
+                 v_dtype: torch.dtype = E4M3):
     """Q/K/V e4m3 quantisation of the drop-in path (``mh3_quantize_qkv``).
 
     Returns (q8, k8, v8, scale_q, scale_k, scale_v, k_mean): q8 [B,H,Sq,D],
     k8/v8 [B,H,Sk,D] contiguous e4m3; scale_q [B,H,ceil(Sq/128)],
     scale_k [B,H,ceil(Sk/128)], scale_v / k_mean [B,H,D] float32.
+    ``v_dtype=torch.float16`` returns v/scale_v in f16 instead of e4m3.
     """
     lib = _lib.load()
     _require_cuda(q, k, v)
@@ -240,7 +248,9 @@ def quantize_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_premul: fl
     q, k, v = tensors
     q8 = torch.empty((B, H, Sq, D), dtype=E4M3, device=dev)
     k8 = torch.empty((B, H, Sk, D), dtype=E4M3, device=dev)
-    v8 = torch.empty((B, H, Sk, D), dtype=E4M3, device=dev)
+    if v_dtype not in (E4M3, torch.float16):
+        raise ValueError("v_dtype must be float8_e4m3fn or float16")
+    v8 = torch.empty((B, H, Sk, D), dtype=v_dtype, device=dev)
     sq = torch.empty((B, H, _cdiv(Sq, BLOCK)), dtype=torch.float32, device=dev)
     sk = torch.empty((B, H, _cdiv(Sk, BLOCK)), dtype=torch.float32, device=dev)
     sv = torch.empty((B, H, D), dtype=torch.float32, device=dev)
@@ -254,6 +264,7 @@ def quantize_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_premul: fl
     a.k, a.k_stride_b, a.k_stride_h, a.k_stride_s = k.data_ptr(), k.stride(0), k.stride(1), k.stride(2)
     a.v, a.v_stride_b, a.v_stride_h, a.v_stride_s = v.data_ptr(), v.stride(0), v.stride(1), v.stride(2)
     a.q_premul = float(q_premul)
+    a.v_out_dtype = _lib.MH3_DTYPE_F16 if v_dtype == torch.float16 else _lib.MH3_DTYPE_E4M3
     a.q8, a.k8, a.v8 = q8.data_ptr(), k8.data_ptr(), v8.data_ptr()
     a.scale_q, a.scale_k, a.scale_v, a.k_mean = sq.data_ptr(), sk.data_ptr(), sv.data_ptr(), kmean.data_ptr()
     a.workspace = ws.data_ptr()
@@ -279,3 +290,19 @@ def quantize_rows(x2d: torch.Tensor):
                                        x8.data_ptr(), scale.data_ptr(), _stream(x2d.device))
         _lib.check(rc, "mh3_quantize_rows")
     return x8, scale
+
+
+def widen_e4m3_to_f16(x8: torch.Tensor) -> torch.Tensor:
+    """Exact e4m3 -> float16 copy of a contiguous tensor (``mh3_widen_e4m3_to_f16``)."""
+    lib = _lib.load()
+    if x8.dtype != E4M3 or not x8.is_cuda:
+        raise ValueError("expected a CUDA float8_e4m3fn tensor")
+    x8 = x8.contiguous()
+    out = torch.empty(x8.shape, dtype=torch.float16, device=x8.device)
+    n = x8.numel()
+    if n % 16 or x8.data_ptr() % 16:
+        return x8.to(torch.float16)
+    with torch.cuda.device(x8.device):
+        rc = lib.mh3_widen_e4m3_to_f16(x8.data_ptr(), out.data_ptr(), n, _stream(x8.device))
+    _lib.check(rc, "mh3_widen_e4m3_to_f16")
+    return out

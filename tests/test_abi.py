@@ -57,11 +57,12 @@ def test_invalid_arguments_are_rejected_without_gpu():
 
 
 def test_struct_sizes_match_c_layout():
-    # AttnArgs: 6 int32, then pointer/int64 fields; see include/mh3_b200.h.
+    # AttnArgs: 8 int32, then pointer/int64 fields; see include/mh3_b200.h.
     assert ctypes.sizeof(_lib.AttnArgs) % 8 == 0
-    assert _lib.AttnArgs.q8.offset == 24
+    assert _lib.AttnArgs.q8.offset == 32
     assert _lib.AttnArgs.logit_scale_log2.offset + 8 == _lib.AttnArgs.cu_seqlens_q.offset
     assert _lib.QkvQuantArgs.q.offset == 24
+    assert _lib.QkvQuantArgs.v_out_dtype.offset == _lib.QkvQuantArgs.q_premul.offset + 4
 
 
 def test_struct_offsets_match_gcc(tmp_path):

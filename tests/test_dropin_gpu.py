@@ -53,7 +53,9 @@ def test_routed_sdpa_takes_fp8_branch():
         out = A.routed_sdpa(q, k, v)
     ref = A._orig_sdpa(q.float(), k.float(), v.float())
     r = OA.compare(out.float().cpu(), ref.cpu())
-    assert r["cos"] > 0.999, r
+    # Against the unquantised inputs the e4m3 input rounding is included.
+    assert r["cos"] > 0.995, r
+    assert not torch.equal(out, A._orig_sdpa(q, k, v))
     # Outside the scope the original SDPA runs.
     out2 = A.routed_sdpa(q, k, v)
     assert torch.equal(out2, A._orig_sdpa(q, k, v))
