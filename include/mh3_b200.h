@@ -161,6 +161,23 @@ typedef struct mh3_qkv_quant_args {
 MH3_API uint64_t mh3_qkv_workspace_bytes(int32_t batch, int32_t heads, int32_t seqlen_k, int32_t head_dim);
 MH3_API int mh3_quantize_qkv(const mh3_qkv_quant_args* args, void* stream);
 
+/*
+ * mh3_quantize_qkv without a caller workspace.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory when
+ * they call this path (a plugin whose enqueue step must not allocate, a
+ * latency-critical loop that cannot afford cudaMalloc's implicit device
+ * synchronisation, a host program whose device memory belongs to another
+ * framework's pool).  It allocates nothing: its scratch is a fixed 8 MiB
+ * array in the library's device image, held by every GPU that loads the
+ * library until exit.  ``args->workspace`` is ignored.  Sizes needing more
+ * than 8 MiB (mh3_qkv_workspace_bytes() > 8 MiB) are rejected with
+ * MH3_ERR_TOO_LARGE.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress, with that device current); make that
+ * first call before any stream capture.  All calls share the array: calls
+ * that overlap on the GPU race and must be serialised.
+ */
+MH3_API int mh3_quantize_qkv_noalloc(const mh3_qkv_quant_args* args, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Per-row e4m3 quantisation                                                 */
 /* ------------------------------------------------------------------------ */

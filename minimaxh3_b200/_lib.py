@@ -75,6 +75,7 @@ _SIGNATURES = {
     "mh3_fp8_attention_fwd": (c_i32, [ctypes.POINTER(AttnArgs), c_ptr]),
     "mh3_qkv_workspace_bytes": (c_u64, [c_i32, c_i32, c_i32, c_i32]),
     "mh3_quantize_qkv": (c_i32, [ctypes.POINTER(QkvQuantArgs), c_ptr]),
+    "mh3_quantize_qkv_noalloc": (c_i32, [ctypes.POINTER(QkvQuantArgs), c_ptr]),
     "mh3_quantize_rows": (c_i32, [c_ptr, c_i64, c_i32, c_i64, c_i64, c_ptr, c_ptr, c_ptr]),
     "mh3_widen_e4m3_to_f16": (c_i32, [c_ptr, c_ptr, c_i64, c_ptr]),
 }

@@ -12,6 +12,8 @@
 //
 // Divisions are IEEE round-to-nearest (``__fdiv_rn``) and the e4m3 cast is
 // RNE after the same +-448 clamp, so the bytes match the CPU restatement.
+#include <mutex>
+
 #include "mh3_internal.h"
 #include "ptx.cuh"
 
@@ -354,4 +356,71 @@ extern "C" int mh3_widen_e4m3_to_f16(const void* src, void* dst, int64_t n, void
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "mh3_widen_e4m3_to_f16 launch");
   return MH3_OK;
+}
+
+// ----------------------------------------------------------------------------
+// mh3_quantize_qkv_noalloc: the same quantisation with library-owned scratch.
+//
+// Some callers cannot allocate device memory when they call this path: a
+// plugin inside another inference runtime whose enqueue step may not allocate
+// (the runtime plans every device buffer up front), a latency-critical
+// serving loop where cudaMalloc's implicit device synchronisation would stall
+// work already in flight, or a host program whose device memory all belongs
+// to another framework's pool.  This entry point takes its K/V statistics
+// scratch from a fixed array in the library's own device image instead of a
+// caller workspace.  It never calls cudaMalloc, cudaFree or any allocating
+// routine.
+//
+// The array is ``kNoAllocScratchBytes`` (8 MiB) and every GPU that loads the
+// library holds it until the process exits.  Every call shares it and it
+// keeps the last call's contents; the statistics kernel writes every partial
+// the finishing kernel reads, so nothing has to start at zero.  Calls that
+// overlap on the GPU (two streams, or two devices' work aimed at one device)
+// race on the array: serialise them.
+// ----------------------------------------------------------------------------
+namespace mh3 {
+namespace quant {
+
+constexpr unsigned long long kNoAllocScratchBytes = 8ull << 20;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on the current device.  In host code
+// the symbol names a host-side stand-in, not device memory, so the address
+// is looked up once per device (with that device current) and cached.
+static int noalloc_scratch(void** out) {
+  constexpr int kMaxDevices = 64;
+  static void* addr[kMaxDevices] = {};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e, "mh3_quantize_qkv_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(MH3_ERR_UNSUPPORTED, "device index out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return fail_cuda(e, "mh3_quantize_qkv_noalloc: cudaGetSymbolAddress");
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return MH3_OK;
+}
+
+}  // namespace quant
+}  // namespace mh3
+
+extern "C" int mh3_quantize_qkv_noalloc(const mh3_qkv_quant_args* a, void* stream) {
+  if (a == nullptr) return fail(MH3_ERR_INVALID, "mh3_quantize_qkv_noalloc: null args");
+  const uint64_t need = mh3_qkv_workspace_bytes(a->batch, a->heads, a->seqlen_k, a->head_dim);
+  if (need > quant::kNoAllocScratchBytes)
+    return fail(MH3_ERR_TOO_LARGE,
+                "mh3_quantize_qkv_noalloc: scratch needed (2*batch*heads*ceil(seqlen_k/256)*head_dim*4 bytes) "
+                "exceeds its fixed 8 MiB; use mh3_quantize_qkv with a caller workspace");
+  void* scratch = nullptr;
+  const int rc = quant::noalloc_scratch(&scratch);
+  if (rc != MH3_OK) return rc;
+  mh3_qkv_quant_args b = *a;
+  b.workspace = scratch;
+  return mh3_quantize_qkv(&b, stream);
 }
