@@ -190,6 +190,49 @@ MH3_API int mh3_quantize_qkv_noalloc(const mh3_qkv_quant_args* args, void* strea
 MH3_API int mh3_quantize_rows(const void* x, int64_t x_stride, int32_t in_dtype, int64_t M, int64_t K, void* x8,
                       float* scale, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Scaled GEMM with fused bias and low-rank (LoRA) epilogue                  */
+/* ------------------------------------------------------------------------ */
+/*
+ * Replaces ``torch._scaled_mm(x8, w8.t(), scale_a=x_scale, scale_b=w_scale,
+ * bias=bias, out_dtype=bf16)`` plus the per-adapter LoRA loop of
+ * ``FP8Linear.forward`` (kernels/fp8_linear.py:95-108, :45-55):
+ *
+ *   out[m,n] = bf16( (sum_k a[m,k]*b[n,k] + sum_r a2[m,r]*b2[n,r])
+ *                    * rs[m] * cs[n] + bias[n] )
+ *
+ * a [M,K], b [N,K]: e4m3 or bf16 (ab_dtype), K contiguous, row strides lda /
+ * ldb in elements (multiples of 16 bytes).  rs = row_scale[m] (or
+ * 1/row_scale[m] with row_scale_inv), cs = col_scale[n]; NULL means 1.  bias:
+ * bf16 [N] or NULL.  a2 [M,R], b2 [N,R]: optional bf16 low-rank operands
+ * accumulated into the same fp32 accumulator (R = 0: none); FP8Linear passes
+ * a2 = (x A^T)/x_scale and b2 = lora_scale*B/w_scale so the epilogue adds
+ * the adapter delta.  out: bf16 [M,N], row stride ldo.  N, ldo, R multiples
+ * of 8.
+ */
+typedef struct mh3_gemm_args {
+  int64_t M, N, K, R;
+  int32_t ab_dtype; /* MH3_DTYPE_E4M3 or MH3_DTYPE_BF16 */
+  int32_t row_scale_inv;
+  const void* a;
+  int64_t lda;
+  const void* b;
+  int64_t ldb;
+  const float* row_scale;
+  const float* col_scale;
+  const void* bias;
+  const void* a2;
+  int64_t lda2;
+  const void* b2;
+  int64_t ldb2;
+  void* out;
+  int64_t ldo;
+  int* err;
+  uint64_t timeout_ns;
+} mh3_gemm_args;
+
+MH3_API int mh3_scaled_gemm(const mh3_gemm_args* args, void* stream);
+
 /*
  * Exact widening of e4m3 to f16 (every e4m3 value is an f16 value): dst[i] =
  * src[i] for n contiguous elements.  Feeds pre-quantised e4m3 V to the

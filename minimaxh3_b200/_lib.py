@@ -67,6 +67,19 @@ class QkvQuantArgs(ctypes.Structure):
     ]
 
 
+class GemmArgs(ctypes.Structure):
+    """``mh3_gemm_args`` (include/mh3_b200.h)."""
+
+    _fields_ = [
+        ("M", c_i64), ("N", c_i64), ("K", c_i64), ("R", c_i64),
+        ("ab_dtype", c_i32), ("row_scale_inv", c_i32),
+        ("a", c_ptr), ("lda", c_i64), ("b", c_ptr), ("ldb", c_i64),
+        ("row_scale", c_ptr), ("col_scale", c_ptr), ("bias", c_ptr),
+        ("a2", c_ptr), ("lda2", c_i64), ("b2", c_ptr), ("ldb2", c_i64),
+        ("out", c_ptr), ("ldo", c_i64), ("err", c_ptr), ("timeout_ns", c_u64),
+    ]
+
+
 # name -> (restype, argtypes)
 _SIGNATURES = {
     "mh3_abi_version": (c_i32, []),
@@ -78,6 +91,7 @@ _SIGNATURES = {
     "mh3_quantize_qkv_noalloc": (c_i32, [ctypes.POINTER(QkvQuantArgs), c_ptr]),
     "mh3_quantize_rows": (c_i32, [c_ptr, c_i64, c_i32, c_i64, c_i64, c_ptr, c_ptr, c_ptr]),
     "mh3_widen_e4m3_to_f16": (c_i32, [c_ptr, c_ptr, c_i64, c_ptr]),
+    "mh3_scaled_gemm": (c_i32, [ctypes.POINTER(GemmArgs), c_ptr]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

@@ -1,0 +1,349 @@
+// Scaled GEMM with a fused epilogue for sm_100a (tcgen05 + TMA).
+//
+// Replaces ``torch._scaled_mm(x8, w8.t(), scale_a, scale_b, bias, bf16)`` and
+// the LoRA adapter loop that follows it in the reference's
+// ``FP8Linear.forward`` (kernels/fp8_linear.py:95-108, :45-55):
+//
+//   out[m,n] = bf16( (sum_k a[m,k] b[n,k] + sum_r a2[m,r] b2[n,r])
+//                    * rs[m] * cs[n] + bias[n] )
+//
+// a, b are e4m3 (kind::f8f6f4) or bf16 (kind::f16), K-major.  The optional
+// low-rank term (a2 [M,R], b2 [N,R], bf16) is accumulated into the same TMEM
+// accumulator after the main K loop; FP8Linear passes a2 = (x A^T)/sa and
+// b2 = scale*B/sb so that the scaled epilogue yields main + LoRA delta.  rs
+// may be replaced by 1/rs (``row_scale_inv``) - the form the LoRA-down
+// product x A^T / sa uses.
+//
+// Persistent kernel, one CTA per SM, 192 threads:
+//   warp 0      TMA producer (4-stage ring of 48 KB stages)
+//   warp 1      MMA issuer; owns 512 TMEM columns = two 256-column accumulators
+//   warps 2-5   epilogue (thread i of the warpgroup owns accumulator row i)
+// The epilogue of one tile overlaps the main loop of the next.  Tiles are
+// visited in groups of kGroupM M-blocks per N-column so the working set of
+// A and B rows stays in L2.  Every mbarrier wait is bounded.
+#include <mutex>
+
+#include "mh3_b200.h"
+#include "mh3_internal.h"
+#include "ptx.cuh"
+
+namespace mh3 {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int STAGES = 4;
+constexpr int STAGE_K_BYTES = 128;  // bytes of K per stage: 128 e4m3 or 64 bf16
+constexpr int kGroupM = 16;
+constexpr int NUM_THREADS = 192;
+
+struct Params {
+  CUtensorMap tma_a;   // (K, M), box (128 B, 128)
+  CUtensorMap tma_b;   // (K, N), box (128 B, BN)
+  CUtensorMap tma_a2;  // bf16 (R, M), box (64, 128)
+  CUtensorMap tma_b2;  // bf16 (R, N), box (64, BN)
+  int M, N, K, R;
+  int bf16_ab;  // main operands are bf16 (else e4m3)
+  const float* rs;
+  int rs_inv;
+  const float* cs;
+  const __nv_bfloat16* bias;
+  __nv_bfloat16* out;
+  long long ldo;
+  int* err;
+  unsigned long long timeout_ns;
+};
+
+template <int BN>
+struct __align__(1024) Smem {
+  uint8_t a[STAGES][BM * STAGE_K_BYTES];
+  uint8_t b[STAGES][BN * STAGE_K_BYTES];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem<BN>& sm = *reinterpret_cast<Smem<BN>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (p.M + BM - 1) / BM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int kst_main = (p.K * (p.bf16_ab ? 2 : 1) + STAGE_K_BYTES - 1) / STAGE_K_BYTES;
+  const int kst_lora = (p.R * 2 + STAGE_K_BYTES - 1) / STAGE_K_BYTES;
+  const int kst = kst_main + kst_lora;
+
+  // tile index -> (m-block, n-block): groups of kGroupM m-blocks sweep all n.
+  auto coords = [&](int t, int& mb, int& nb) {
+    const int per_group = kGroupM * num_n;
+    const int g = t / per_group;
+    const int r = t - g * per_group;
+    const int gm = min(kGroupM, num_m - g * kGroupM);
+    nb = r / gm;
+    mb = g * kGroupM + (r - nb * gm);
+  };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(smem_u32(&sm.full[i]), 1);
+      mbar_init(smem_u32(&sm.empty[i]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&sm.acc_full[i]), 1);
+      mbar_init(smem_u32(&sm.acc_empty[i]), 4);
+    }
+    mbar_init(smem_u32(&sm.mma_done), 1);
+    sm.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&sm.tmem_base), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  const WaitGuard g{&sm.abort_flag, p.err, p.timeout_ns};
+  constexpr uint32_t kStageBytes = (BM + BN) * STAGE_K_BYTES;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------------- producer
+      tma_prefetch_desc(&p.tma_a);
+      tma_prefetch_desc(&p.tma_b);
+      if (p.R > 0) {
+        tma_prefetch_desc(&p.tma_a2);
+        tma_prefetch_desc(&p.tma_b2);
+      }
+      int it = 0;
+      int last_issued = -1;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        coords(t, mb, nb);
+        for (int s = 0; s < kst; ++s, ++it) {
+          const int st = it % STAGES;
+          if (!mbar_wait(smem_u32(&sm.empty[st]), ((uint32_t)(it / STAGES) & 1u) ^ 1u, g)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&sm.full[st]);
+          mbar_arrive_expect_tx(fb, kStageBytes);
+          if (s < kst_main) {
+            const int kc = s * (p.bf16_ab ? STAGE_K_BYTES / 2 : STAGE_K_BYTES);
+            tma_load_2d(smem_u32(sm.a[st]), &p.tma_a, fb, kc, mb * BM);
+            tma_load_2d(smem_u32(sm.b[st]), &p.tma_b, fb, kc, nb * BN);
+          } else {
+            const int rc = (s - kst_main) * (STAGE_K_BYTES / 2);
+            tma_load_2d(smem_u32(sm.a[st]), &p.tma_a2, fb, rc, mb * BM);
+            tma_load_2d(smem_u32(sm.b[st]), &p.tma_b2, fb, rc, nb * BN);
+          }
+          last_issued = it;
+        }
+      }
+      // Teardown: the last copy issued into each stage must land.
+      for (int i = max(0, last_issued - STAGES + 1); i <= last_issued; ++i)
+        mbar_wait_teardown(smem_u32(&sm.full[i % STAGES]), (uint32_t)(i / STAGES) & 1u, p.timeout_ns);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------------------------------------------- MMA issuer
+      constexpr uint32_t kIdF8 = idesc_e4m3(BM, BN, false, false);
+      constexpr uint32_t kIdBF = idesc_bf16(BM, BN, false, false);
+      int it = 0, tcount = 0;
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tcount) {
+        const int acc = tcount & 1;
+        const uint32_t d_tmem = tmem + (uint32_t)(acc * 256);
+        mbar_wait(smem_u32(&sm.acc_empty[acc]), ((uint32_t)(tcount >> 1) & 1u) ^ 1u, g);
+        tc_fence_after();
+        for (int s = 0; s < kst; ++s, ++it) {
+          const int st = it % STAGES;
+          mbar_wait(smem_u32(&sm.full[st]), (uint32_t)(it / STAGES) & 1u, g);
+          tc_fence_after();
+          const uint32_t ab = smem_u32(sm.a[st]);
+          const uint32_t bb = smem_u32(sm.b[st]);
+          const bool f16kind = (s >= kst_main) || p.bf16_ab;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {  // 32 bytes of K per MMA
+            const uint64_t ad = smem_desc(ab + kk * 32, 16, 1024, kLayoutSW128);
+            const uint64_t bd = smem_desc(bb + kk * 32, 16, 1024, kLayoutSW128);
+            const uint32_t accum = (s > 0 || kk > 0) ? 1u : 0u;
+            if (f16kind)
+              mma_f16_ss(d_tmem, ad, bd, kIdBF, accum);
+            else
+              mma_f8_ss(d_tmem, ad, bd, kIdF8, accum);
+          }
+          mma_commit(smem_u32(&sm.empty[st]));
+        }
+        mma_commit(smem_u32(&sm.acc_full[acc]));
+      }
+      // Every MMA must be finished before the CTA frees TMEM (also on the
+      // abort path, where the epilogue's waits return early).
+      mma_commit(smem_u32(&sm.mma_done));
+      mbar_wait_teardown(smem_u32(&sm.mma_done), 0, p.timeout_ns);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    int tcount = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tcount) {
+      int mb, nb;
+      coords(t, mb, nb);
+      const int acc = tcount & 1;
+      mbar_wait(smem_u32(&sm.acc_full[acc]), (uint32_t)(tcount >> 1) & 1u, g);
+      tc_fence_after();
+      const int m = mb * BM + row;
+      const bool row_ok = m < p.M;
+      float rsv = 1.0f;
+      if (p.rs != nullptr && row_ok) rsv = p.rs_inv ? 1.0f / __ldg(p.rs + m) : __ldg(p.rs + m);
+      __nv_bfloat16* orow = p.out + (long long)(row_ok ? m : 0) * p.ldo;
+      const int n0 = nb * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + (uint32_t)(acc * 256 + c * 32) + lane_off, v);
+        tmem_wait_ld();
+        const int nc = n0 + c * 32;
+        if (nc >= p.N) continue;
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int n = nc + 2 * i;
+          float x0 = __uint_as_float(v[2 * i]) * rsv;
+          float x1 = __uint_as_float(v[2 * i + 1]) * rsv;
+          if (p.cs != nullptr) {
+            x0 *= (n < p.N) ? __ldg(p.cs + n) : 0.0f;
+            x1 *= (n + 1 < p.N) ? __ldg(p.cs + n + 1) : 0.0f;
+          }
+          if (p.bias != nullptr) {
+            x0 += (n < p.N) ? __bfloat162float(p.bias[n]) : 0.0f;
+            x1 += (n + 1 < p.N) ? __bfloat162float(p.bias[n + 1]) : 0.0f;
+          }
+          __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+          packed[i] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            if (nc + 8 * i < p.N)  // N is a multiple of 8
+              *reinterpret_cast<uint4*>(orow + nc + 8 * i) =
+                  make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sm.acc_empty[acc]));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int BN>
+constexpr uint32_t smem_bytes() {
+  return (uint32_t)sizeof(Smem<BN>) + 1024;
+}
+
+// 2-D K-major map: dims (K, rows), box (box_k elements, box_rows), swizzle 128B.
+static int make_map_2d(CUtensorMap* map, const void* base, bool bf16, long long K, long long rows,
+                       long long ld_elems, int box_rows) {
+  const long long es = bf16 ? 2 : 1;
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(ld_elems * es)};
+  const cuuint32_t box[2] = {(cuuint32_t)(STAGE_K_BYTES / es), (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1u, 1u};
+  return encode_tiled(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                      const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <int BN>
+static cudaError_t launch(const Params& p, cudaStream_t st) {
+  auto kern = gemm_kernel<BN>;
+  static std::once_flag once;
+  static cudaError_t attr = cudaSuccess;
+  std::call_once(once, [&] {
+    attr = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes<BN>());
+  });
+  if (attr != cudaSuccess) return attr;
+  int dev = 0, nsm = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  const long long tiles = (long long)((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
+  const int grid = (int)(tiles < nsm ? tiles : nsm);
+  kern<<<grid, NUM_THREADS, smem_bytes<BN>(), st>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace gemm
+}  // namespace mh3
+
+using namespace mh3;
+
+extern "C" int mh3_scaled_gemm(const mh3_gemm_args* a, void* stream) {
+  if (a == nullptr) return fail(MH3_ERR_INVALID, "mh3_scaled_gemm: null args");
+  if (a->M < 0 || a->N <= 0 || a->K <= 0) return fail(MH3_ERR_INVALID, "sizes must be positive");
+  if (a->M == 0) return MH3_OK;
+  if (a->M > 0x7fffffffLL || a->N > 0x7fffffffLL || a->K > 0x7fffffffLL || a->R > 0x7fffffffLL)
+    return fail(MH3_ERR_TOO_LARGE, "dimension too large");
+  if (a->ab_dtype != MH3_DTYPE_E4M3 && a->ab_dtype != MH3_DTYPE_BF16)
+    return fail(MH3_ERR_INVALID, "ab_dtype must be e4m3 or bf16");
+  const bool bf16 = a->ab_dtype == MH3_DTYPE_BF16;
+  const long long es = bf16 ? 2 : 1;
+  if (!a->a || !a->b || !a->out) return fail(MH3_ERR_INVALID, "null a/b/out");
+  if ((a->K * es) % 16 || (a->lda * es) % 16 || (a->ldb * es) % 16)
+    return fail(MH3_ERR_INVALID, "K and the row strides of a and b must be multiples of 16 bytes");
+  if (a->N % 8 || a->ldo % 8) return fail(MH3_ERR_INVALID, "N and ldo must be multiples of 8");
+  auto al16 = [](const void* p_) { return ((uintptr_t)p_ & 15u) == 0; };
+  if (!al16(a->a) || !al16(a->b) || !al16(a->out)) return fail(MH3_ERR_INVALID, "a/b/out must be 16-byte aligned");
+  if (a->R < 0) return fail(MH3_ERR_INVALID, "R must be >= 0");
+  if (a->R > 0) {
+    if (!a->a2 || !a->b2) return fail(MH3_ERR_INVALID, "R > 0 needs a2 and b2");
+    if (a->R % 8 || a->lda2 % 8 || a->ldb2 % 8 || !al16(a->a2) || !al16(a->b2))
+      return fail(MH3_ERR_INVALID, "R and the strides of a2/b2 must be multiples of 8 (16 bytes), 16-byte aligned");
+  }
+  gemm::Params p;
+  memset(&p, 0, sizeof(p));
+  const int BN = a->N <= 64 ? 64 : 256;
+  int rc = gemm::make_map_2d(&p.tma_a, a->a, bf16, a->K, a->M, a->lda, gemm::BM);
+  if (rc) return rc;
+  rc = gemm::make_map_2d(&p.tma_b, a->b, bf16, a->K, a->N, a->ldb, BN);
+  if (rc) return rc;
+  if (a->R > 0) {
+    rc = gemm::make_map_2d(&p.tma_a2, a->a2, true, a->R, a->M, a->lda2, gemm::BM);
+    if (rc) return rc;
+    rc = gemm::make_map_2d(&p.tma_b2, a->b2, true, a->R, a->N, a->ldb2, BN);
+    if (rc) return rc;
+  }
+  p.M = (int)a->M;
+  p.N = (int)a->N;
+  p.K = (int)a->K;
+  p.R = (int)a->R;
+  p.bf16_ab = bf16 ? 1 : 0;
+  p.rs = a->row_scale;
+  p.rs_inv = a->row_scale_inv;
+  p.cs = a->col_scale;
+  p.bias = static_cast<const __nv_bfloat16*>(a->bias);
+  p.out = static_cast<__nv_bfloat16*>(a->out);
+  p.ldo = a->ldo;
+  p.err = a->err ? a->err : device_error_word();
+  p.timeout_ns = a->timeout_ns ? a->timeout_ns : 4000000000ull;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const cudaError_t e = BN == 64 ? gemm::launch<64>(p, st) : gemm::launch<256>(p, st);
+  if (e != cudaSuccess) return fail_cuda(e, "mh3_scaled_gemm launch");
+  return MH3_OK;
+}

@@ -306,3 +306,100 @@ def widen_e4m3_to_f16(x8: torch.Tensor) -> torch.Tensor:
         rc = lib.mh3_widen_e4m3_to_f16(x8.data_ptr(), out.data_ptr(), n, _stream(x8.device))
     _lib.check(rc, "mh3_widen_e4m3_to_f16")
     return out
+
+
+# ---------------------------------------------------------------------------
+# scaled GEMM / FP8 linear
+# ---------------------------------------------------------------------------
+
+
+def scaled_gemm(a: torch.Tensor, b: torch.Tensor, row_scale=None, col_scale=None, bias=None, a2=None, b2=None,
+                row_scale_inv: bool = False, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``mh3_scaled_gemm``: bf16 (a b^T [+ a2 b2^T]) * rs[m] * cs[n] + bias[n].
+
+    a [M,K], b [N,K]: both float8_e4m3fn or both bfloat16, last dim
+    contiguous.  row_scale [M] / [M,1], col_scale [N] / [1,N] float32; bias
+    bf16 [N]; a2 [M,R], b2 [N,R] bf16 (optional low-rank term).
+    """
+    lib = _lib.load()
+    _require_cuda(a, b)
+    if a.dtype != b.dtype or a.dtype not in (E4M3, torch.bfloat16):
+        raise ValueError("a and b must both be float8_e4m3fn or both bfloat16")
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[1]:
+        raise ValueError("a is [M,K] and b is [N,K]")
+    M, K = a.shape
+    N = b.shape[0]
+    if a.stride(1) != 1 or b.stride(1) != 1:
+        raise ValueError("a and b need a contiguous last dimension")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    g = _lib.GemmArgs()
+    g.M, g.N, g.K = M, N, K
+    g.ab_dtype = _lib.MH3_DTYPE_BF16 if a.dtype == torch.bfloat16 else _lib.MH3_DTYPE_E4M3
+    g.row_scale_inv = 1 if row_scale_inv else 0
+    g.a, g.lda, g.b, g.ldb = a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0)
+    keep = []
+    for name, t, n in (("row_scale", row_scale, M), ("col_scale", col_scale, N)):
+        if t is not None:
+            t = t.reshape(-1)
+            if t.dtype != torch.float32 or t.numel() != n:
+                raise ValueError(f"{name} must be float32 with {n} elements")
+            t = t.contiguous()
+            keep.append(t)
+            setattr(g, name, t.data_ptr())
+    if bias is not None:
+        bias = bias.reshape(-1).to(torch.bfloat16).contiguous()
+        if bias.numel() != N:
+            raise ValueError("bias must have N elements")
+        keep.append(bias)
+        g.bias = bias.data_ptr()
+    if a2 is not None:
+        if b2 is None or a2.dtype != torch.bfloat16 or b2.dtype != torch.bfloat16:
+            raise ValueError("a2/b2 must both be bfloat16")
+        if a2.shape[0] != M or b2.shape[0] != N or a2.shape[1] != b2.shape[1]:
+            raise ValueError("a2 is [M,R] and b2 is [N,R]")
+        g.R = a2.shape[1]
+        g.a2, g.lda2, g.b2, g.ldb2 = a2.data_ptr(), a2.stride(0), b2.data_ptr(), b2.stride(0)
+    g.out, g.ldo = out.data_ptr(), out.stride(0)
+    with torch.cuda.device(a.device):
+        rc = lib.mh3_scaled_gemm(g, _stream(a.device))
+    _lib.check(rc, "mh3_scaled_gemm")
+    return out
+
+
+def _round_up(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+def fp8_linear(x2d: torch.Tensor, w8: torch.Tensor, w_scale: torch.Tensor, bias, adapters) -> torch.Tensor:
+    """FP8Linear forward: per-token e4m3 activations, one fused GEMM (bf16 out).
+
+    ``adapters``: list of (A [r,K], B [N,r], scale).  Their delta
+    ``scale * (x A^T) B^T`` (on the unquantised x, fp8_linear.py:45-55) is
+    folded into the GEMM: a2 = (x A_cat^T) / x_scale and
+    b2 = (scale*B)_cat / w_scale, both bf16, accumulated with the e4m3
+    product before the row/column scales are applied.
+    """
+    if x2d.dtype not in (torch.bfloat16, torch.float16):
+        x2d = x2d.to(torch.bfloat16)
+    x2d = x2d.contiguous()
+    M, K = x2d.shape
+    N = w8.shape[0]
+    x8, sa = quantize_rows(x2d)
+    sb = w_scale.reshape(-1).float()
+    a2 = b2 = None
+    if adapters:
+        xb = x2d if x2d.dtype == torch.bfloat16 else x2d.to(torch.bfloat16)
+        R = sum(int(A.shape[0]) for A, _, _ in adapters)
+        Rp = _round_up(max(R, 1), 16)
+        A_cat = torch.zeros((Rp, K), dtype=torch.bfloat16, device=x2d.device)
+        B_cat = torch.zeros((N, Rp), dtype=torch.float32, device=x2d.device)
+        r0 = 0
+        for A, B_, s in adapters:
+            r = int(A.shape[0])
+            A_cat[r0:r0 + r] = A.to(torch.bfloat16)
+            B_cat[:, r0:r0 + r] = B_.float() * float(s)
+            r0 += r
+        b2 = (B_cat / sb[:, None]).to(torch.bfloat16)
+        a2 = scaled_gemm(xb, A_cat, row_scale=sa, row_scale_inv=True)
+    return scaled_gemm(x8, w8, row_scale=sa, col_scale=sb, bias=bias, a2=a2, b2=b2)

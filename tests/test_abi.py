@@ -74,7 +74,9 @@ def test_struct_offsets_match_gcc(tmp_path):
     if cc is None:
         pytest.skip("no C compiler")
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "mh3_b200.h"', "int main(void){"]
-    for cname, cls in (("mh3_attn_args", _lib.AttnArgs), ("mh3_qkv_quant_args", _lib.QkvQuantArgs)):
+    structs = (("mh3_attn_args", _lib.AttnArgs), ("mh3_qkv_quant_args", _lib.QkvQuantArgs),
+               ("mh3_gemm_args", _lib.GemmArgs))
+    for cname, cls in structs:
         lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
         for fname, _ in cls._fields_:
             lines.append(f'printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
@@ -89,7 +91,7 @@ def test_struct_offsets_match_gcc(tmp_path):
         if line:
             parts = line.split()
             got[(parts[0], parts[1])] = int(parts[2])
-    for cname, cls in (("mh3_attn_args", _lib.AttnArgs), ("mh3_qkv_quant_args", _lib.QkvQuantArgs)):
+    for cname, cls in structs:
         assert got[(cname, "size")] == ctypes.sizeof(cls)
         for fname, _ in cls._fields_:
             assert got[(cname, fname)] == getattr(cls, fname).offset, (cname, fname)
