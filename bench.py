@@ -13,8 +13,12 @@ larger than the 126 MB L2).  ``e2e`` times the drop-in
 ``kernels.fp8_attention.fp8_attention`` on bf16 tensors copied from pinned
 host memory each step, output copied back.
 
-N>1 (torchrun): every rank runs the same single-GPU workload on its own GPU
-(replicas, no collective); ``value`` = all ranks' FLOPs / max-over-ranks time.
+N>1 (torchrun): BASELINE config 5, the sharded configuration - S=75600 H=40
+D=128 self-attention with Ulysses head parallelism (per-(b,h) scales
+all-reduced, e4m3 q/k and f16 v all-to-all over NCCL, local FP8 attention
+over H/N heads, bf16 all-to-all back), then cross-attention of the local
+query shard to 512 replicated text tokens.  ``value`` = total FLOPs of both
+attentions / max-over-ranks device time ("strong" scaling: total work fixed).
 
 ``--impl reference``: the reference's CPU implementation of this path
 (``routed_sdpa`` falling back to torch SDPA on CPU tensors,
@@ -196,7 +200,112 @@ def run_reference_arm(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_ulysses_arm(args, dist, rank, world, local):
+    from minimaxh3_b200.kernels.fp8_attention import fp8_attention
+    from minimaxh3_b200.ulysses import ulysses_attention
+
+    dev = torch.device("cuda", local)
+    S5, H5, D5, T = 75600, 40, 128, 512
+    Sl = S5 // world
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    gc = torch.Generator().manual_seed(0)
+    shard = []
+    for _ in range(3):
+        x = torch.randn(1, Sl, H5, D5, generator=g, device=dev)
+        x[..., int(torch.randperm(D5, generator=gc)[0])] *= 8.0
+        shard.append(x.to(torch.bfloat16))
+    q, k, v = shard
+    gt = torch.Generator(device=dev).manual_seed(7)
+    kt, vt = (torch.randn(1, H5, T, D5, generator=gt, device=dev).to(torch.bfloat16) for _ in range(2))
+    flop_self = 4.0 * H5 * S5 * S5 * D5
+    flop_cross = 4.0 * H5 * S5 * T * D5
+    stream = torch.cuda.current_stream(dev)
+    attn_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+
+    def step(ev=None):
+        o = ulysses_attention(q, k, v, events=ev)
+        c = fp8_attention(q.transpose(1, 2), kt, vt)
+        return o, c
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        t0.record(stream)
+        for i in range(args.steps):
+            step(attn_ev[i])
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    dist.barrier()
+    ms = t0.elapsed_time(t1)
+    attn_ms = sum(a.elapsed_time(b) for a, b in attn_ev) / args.steps
+    t = torch.tensor([ms, attn_ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, attn_ms = float(t[0]), float(t[1])
+    value = (flop_self + flop_cross) * args.steps / (ms / 1e3) / 1e12
+    achieved = flop_self / world / (attn_ms / 1e3) / 1e12
+    peaks = _peaks()
+    # e2e: the local shard comes from pinned host memory and the output goes back
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    ho = torch.empty_like(hq).pin_memory()
+    hc = torch.empty((1, H5, Sl, D5), dtype=torch.bfloat16).pin_memory()
+    dq, dk, dv = (torch.empty_like(x) for x in (q, k, v))
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        o = ulysses_attention(dq, dk, dv)
+        c = fp8_attention(dq.transpose(1, 2), kt, vt)
+        ho.copy_(o, non_blocking=True)
+        hc.copy_(c, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    n_e2e = max(1, min(args.steps, 3))
+    e0.record(stream)
+    for _ in range(n_e2e):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t[0])
+    if rank != 0:
+        return
+    line = {
+        "metric": "FP8 attention TFLOPS (S=32760 H=40 D=128)",
+        "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "e4m3 QK^T, f16 PV", "data": "synthetic",
+        "config": {"workload": f"config5: Ulysses self-attention B=1 H=40 S=75600 D=128 over {world} GPUs "
+                               f"(S/P={Sl}, H/P={H5 // world}) + cross-attention to 512 text tokens",
+                   "parallelism": f"ulysses{world}", "inputs_vs_l2": "per-rank inputs > 126 MB L2 (no flush)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["fp8_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / peaks["fp8_tflops"], "traffic": None, "peak_source": peaks["source"],
+                     "kernel": "mh3::attn::fwd_kernel (local head shard)", "avg_launch_ms": attn_ms},
+        "e2e": {"value": (flop_self + flop_cross) * n_e2e / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": 3 * Sl * H5 * D5 * 2 * world,
+                "d2h_bytes_per_step": 2 * Sl * H5 * D5 * 2 * world,
+                "api": "minimaxh3_b200.ulysses.ulysses_attention + kernels.fp8_attention.fp8_attention"},
+        # per step: local attention + the cross-attention's 5 quantisation
+        # kernels and 1 attention kernel
+        "gpu_launches": 7 * args.steps, "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_gpu_arm(args, dist, rank, world, local):
+    if world > 1:
+        return run_ulysses_arm(args, dist, rank, world, local)
     global H
     H = args.heads
     FLOP_PER_CALL = 4.0 * B * H * S * S * D
@@ -329,6 +438,70 @@ def run_gpu_arm(args, dist, rank, world, local):
     print(json.dumps(line), flush=True)
 
 
+def _time_cuda(fn, steps, warmup, stream):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_linear_workload(args):
+    """FP8 scaled linear with fused epilogue (not the headline).
+
+    M=32760 tokens, K=5120, N in {5120, 15360, 13824}; x N(0,1) bf16, W N(0,0.02),
+    bias N(0,0.01), one LoRA adapter of rank 32 (A, B ~ N(0,0.01), scale 1).
+    Reports, per N: the fused GEMM alone (e4m3 inputs resident), the whole
+    FP8Linear.forward (row quantisation + LoRA-down + fused GEMM), and the
+    reference's GPU recipe on the same box (our row quantisation +
+    torch._scaled_mm + the two LoRA matmuls and the add, fp8_linear.py:87-108).
+    """
+    from minimaxh3_b200 import ops
+    from minimaxh3_b200.kernels.fp8_linear import FP8Linear
+
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    M, K = 32760, 5120
+    x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+    lines = []
+    peaks = _peaks()
+    for N in (5120, 15360, 13824):
+        lin = torch.nn.Linear(K, N, device=dev, dtype=torch.bfloat16)
+        with torch.no_grad():
+            lin.weight.copy_(torch.randn(N, K, generator=g, device=dev) * 0.02)
+            lin.bias.copy_(torch.randn(N, generator=g, device=dev) * 0.01)
+        mod = FP8Linear.from_linear(lin)
+        A = (torch.randn(32, K, generator=g, device=dev) * 0.01).to(torch.bfloat16)
+        Bm = (torch.randn(N, 32, generator=g, device=dev) * 0.01).to(torch.bfloat16)
+        mod.adapters = [(A, Bm, 1.0)]
+        x8, sa = ops.quantize_rows(x)
+        sb = mod.w_scale.reshape(-1)
+        flop = 2.0 * M * N * K
+        t_gemm = _time_cuda(lambda: ops.scaled_gemm(x8, mod.w8, row_scale=sa, col_scale=sb, bias=mod.bias),
+                            args.steps, args.warmup, stream)
+        t_fwd = _time_cuda(lambda: mod(x), args.steps, args.warmup, stream)
+
+        def ref_recipe():
+            out = torch._scaled_mm(x8, mod.w8.t(), scale_a=sa, scale_b=mod.w_scale, bias=mod.bias,
+                                   out_dtype=torch.bfloat16)
+            return out + ((x @ A.t()) @ Bm.t()).to(out.dtype)
+
+        t_ref = _time_cuda(ref_recipe, args.steps, args.warmup, stream)
+        lines.append({"N": N, "gemm_ms": t_gemm, "gemm_tflops": flop / t_gemm / 1e9,
+                      "gemm_frac_of_fp8_peak": flop / t_gemm / 1e9 / peaks["fp8_tflops"],
+                      "fp8linear_forward_ms": t_fwd, "fp8linear_forward_tflops": flop / t_fwd / 1e9,
+                      "reference_recipe_ms": t_ref, "reference_recipe_tflops": flop / t_ref / 1e9})
+    print(json.dumps({"workload": "config4: FP8 scaled linear M=32760 K=5120, LoRA r=32", "unit": "TFLOP/s",
+                      "peak": peaks, "results": lines}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -339,6 +512,8 @@ def main():
     ap.add_argument("--heads", type=int, default=40, help="heads (40 = config 2; fewer for ncu captures)")
     ap.add_argument("--no-extras", action="store_true",
                     help="kernel timing only (no e2e, no CPU baseline): the ncu capture command")
+    ap.add_argument("--workload", default="attention", choices=["attention", "linear"],
+                    help="attention = config 2 (the headline line); linear = config 4 measurements")
     ap.add_argument("--pv", default="f16", choices=["f16", "e4m3"],
                     help="PV product operands: f16 P/V (default, meets the tolerance) or e4m3")
     args = ap.parse_args()
@@ -347,6 +522,9 @@ def main():
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         run_reference_arm(args, rank)
+        return
+    if args.workload == "linear":
+        run_linear_workload(args)
         return
     dist, rank, world, local = _dist()
     try:

@@ -1,0 +1,119 @@
+"""Ulysses (head-parallel) sharding of FP8 attention over NCCL.
+
+The reference runs one GPU per container and has no sequence or head
+parallelism; BASELINE config 5 asks for S=75600 self-attention sharded over
+2/4/8 GPUs.  Each rank holds a contiguous sequence shard of q, k, v
+``[B, S_local, H, D]`` (the layout a sequence-parallel DiT block holds).  Per
+call:
+
+1. per-(batch, head) absmax of the local shard, one ``all_reduce(MAX)`` of
+   3*B*H floats, so every rank quantises with the global per-(b,h) scale
+   (BASELINE configs 2/3/5 use per-(b,h) scales);
+2. local e4m3 quantisation (V: f16 V/scale for the f16 PV product, or e4m3)
+   straight into the send layout ``[P, B, S_local, H/P, D]``;
+3. one NCCL ``all_to_all_single`` per tensor: rank r receives every rank's
+   tokens for heads ``[r*H/P, (r+1)*H/P)``; for B = 1 the receive buffer is
+   already ``[S, H/P, D]`` in global token order and the attention kernel
+   reads it in place through its strided TMA maps;
+4. local FP8 attention over H/P heads, written as ``[P, S_local, H/P, D]``;
+5. one bf16 ``all_to_all_single`` back and a head interleave to
+   ``[B, S_local, H, D]``.
+
+Only steps 1, 3 and 5 communicate; the e4m3 all-to-all moves half the bytes
+of a bf16 one.  Cross-attention to replicated text K/V needs no collective:
+call ``fp8_attention`` on the local query shard.
+
+``attn_fn`` is injectable so the collective plumbing can be tested on CPU
+``gloo`` ranks with the oracle standing in for the kernel.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+LOG2E = 1.4426950408889634
+E4M3 = torch.float8_e4m3fn
+
+
+def _world(group):
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+def global_absmax(xs, group=None):
+    """[len(xs), B, H] float32 absmax over (S, D) of each [B,S_local,H,D], max-reduced over ranks."""
+    local = torch.stack([x.float().abs().amax(dim=(1, 3)) for x in xs])
+    dist.all_reduce(local, op=dist.ReduceOp.MAX, group=group)
+    return local
+
+
+def _quant_to_send(x, scale, P, out_dtype):
+    """x [B,S_l,H,D] / scale[B,H] -> [P, B, S_l, H/P, D] (e4m3 clamp or f16)."""
+    B, S_l, H, D = x.shape
+    y = x.float() / scale[:, None, :, None]
+    if out_dtype == E4M3:
+        y = torch.clamp(y, -448.0, 448.0)
+    y = y.to(out_dtype)
+    return y.reshape(B, S_l, P, H // P, D).permute(2, 0, 1, 3, 4).contiguous()
+
+
+def _exchange(send, group):
+    """all_to_all_single on the leading (rank) dimension; dtype-agnostic."""
+    recv = torch.empty_like(send)
+    s8 = send.view(torch.uint8) if send.dtype == E4M3 else send
+    r8 = recv.view(torch.uint8) if recv.dtype == E4M3 else recv
+    dist.all_to_all_single(r8, s8, group=group)
+    return recv
+
+
+def _head_major(recv):
+    """[P(src), B, S_l, Hl, D] -> [B, Hl, S, D] view (copy only when B > 1)."""
+    P, B, S_l, Hl, D = recv.shape
+    if B == 1:
+        return recv.view(P * S_l, Hl, D).permute(1, 0, 2).unsqueeze(0)  # strided, no copy
+    return recv.permute(1, 3, 0, 2, 4).reshape(B, Hl, P * S_l, D)
+
+
+def _default_attn(q8, k8, v, sq, sk, sv, logit_scale_log2):
+    from . import ops
+
+    return ops.attention_e4m3(q8, k8, v, sq, sk, sv, logit_scale_log2=logit_scale_log2)
+
+
+def ulysses_attention(q, k, v, group=None, scale=None, pv_dtype=torch.float16, attn_fn=None, events=None):
+    """Head-parallel FP8 attention of sequence shards ``[B, S_local, H, D]``.
+
+    Returns the local output shard ``[B, S_local, H, D]`` (bf16, like q's
+    dtype).  H must be divisible by the world size; every rank must hold the
+    same S_local.  ``events``: optional (start, end) CUDA events recorded
+    around the local attention kernel.
+    """
+    P, r = _world(group)
+    B, S_l, H, D = q.shape
+    if H % P:
+        raise ValueError(f"heads ({H}) must be divisible by the world size ({P})")
+    Hl = H // P
+    amax = global_absmax((q, k, v), group)                 # [3, B, H]
+    scales = torch.clamp(amax, min=1e-12) / 448.0
+    sq_full, sk_full, sv_full = scales[0], scales[1], scales[2]
+    send_q = _quant_to_send(q, sq_full, P, E4M3)
+    send_k = _quant_to_send(k, sk_full, P, E4M3)
+    send_v = _quant_to_send(v, sv_full, P, pv_dtype)
+    recv_q, recv_k, recv_v = (_exchange(t, group) for t in (send_q, send_k, send_v))
+    hs = slice(r * Hl, (r + 1) * Hl)
+    sq = sq_full[:, hs].contiguous()[..., None]            # [B, Hl, 1] per-(b,h)
+    sk = sk_full[:, hs].contiguous()[..., None]
+    sv = sv_full[:, hs].contiguous()[..., None]
+    ls2 = (scale if scale is not None else 1.0 / math.sqrt(D)) * LOG2E
+    fn = attn_fn or _default_attn
+    hq, hk, hv = _head_major(recv_q), _head_major(recv_k), _head_major(recv_v)
+    if events is not None:
+        events[0].record()
+    o = fn(hq, hk, hv, sq, sk, sv, ls2)  # [B,Hl,S,D]
+    if events is not None:
+        events[1].record()
+    # send back: chunk p = tokens of rank p -> [P, B, S_l, Hl, D]
+    send_o = o.to(q.dtype).permute(2, 0, 1, 3).reshape(P, S_l, B, Hl, D).permute(0, 2, 1, 3, 4).contiguous()
+    recv_o = _exchange(send_o, group)                       # [P(src heads), B, S_l, Hl, D]
+    return recv_o.permute(1, 2, 0, 3, 4).reshape(B, S_l, H, D)

@@ -1,0 +1,86 @@
+"""Ulysses over NCCL on 2 GPUs: bit-identical to one GPU over the whole sequence.
+
+Every rank quantises with the global per-(batch, head) scales, so the head
+shard each rank attends over holds exactly the bytes a single GPU would use;
+the kernel then computes each head independently.  Skipped with fewer than
+two GPUs.  NVLS is switched off (plain NCCL peer transfers).
+"""
+import math
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs(B, S, H, D):
+    g = torch.Generator().manual_seed(3)
+    xs = []
+    for _ in range(3):
+        x = torch.randn(B, S, H, D, generator=g)
+        x[..., 7] *= 8.0
+        xs.append(x.to(torch.bfloat16))
+    return xs
+
+
+def _worker(rank, world, port, shape, out_dir):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from minimaxh3_b200.ulysses import ulysses_attention
+
+        B, S, H, D = shape
+        q, k, v = (t.cuda() for t in _inputs(B, S, H, D))
+        Sl = S // world
+        sl = slice(rank * Sl, (rank + 1) * Sl)
+        out = ulysses_attention(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous())
+        torch.cuda.synchronize()
+        torch.save(out.cpu(), os.path.join(out_dir, f"out{rank}.pt"))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ulysses_two_gpus_bit_identical(tmp_path):
+    from minimaxh3_b200 import ops
+
+    B, S, H, D = 1, 2 * 1920, 8, 128
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, (B, S, H, D), str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0
+    got = torch.cat([torch.load(tmp_path / f"out{r}.pt") for r in range(2)], dim=1)
+    # one GPU, whole sequence, same global per-(b,h) scales
+    q, k, v = (t.cuda() for t in _inputs(B, S, H, D))
+    ops_in = []
+    scales = []
+    for x, dt in ((q, torch.float8_e4m3fn), (k, torch.float8_e4m3fn), (v, torch.float16)):
+        s = torch.clamp(x.float().abs().amax(dim=(1, 3)), min=1e-12) / 448.0
+        y = x.float() / s[:, None, :, None]
+        if dt == torch.float8_e4m3fn:
+            y = torch.clamp(y, -448, 448)
+        ops_in.append(y.to(dt).permute(0, 2, 1, 3).contiguous())
+        scales.append(s[..., None].contiguous())
+    ref = ops.attention_e4m3(*ops_in, *scales, logit_scale_log2=1.4426950408889634 / math.sqrt(D))
+    ref = ref.permute(0, 2, 1, 3).cpu()
+    assert torch.equal(got, ref)
