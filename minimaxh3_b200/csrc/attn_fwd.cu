@@ -19,14 +19,18 @@
 //  * MMA order  S0(0) S1(0) | PV0(j) S0(j+1) PV1(j) S1(j+1) ... : the tensor
 //    core works on one Q tile while the other tile's softmax runs.
 //  * softmax: exp2 with the dequant scales folded into one FMA per element,
-//    P = e4m3(2^(s*c - m + P_OFFSET)) via packed f16x2 ex2; the running max m
-//    is raised lazily (only when a tile's max exceeds it by LAZY_T, the idea
-//    of the reference's ``rowmax > m + 8`` at :267), and the rare O rescale is
-//    done in TMEM by the softmax warp itself before it releases P.
+//    P = 2^(s*c - m + offset) as f16 (or e4m3); the exp2 pairs are split
+//    between MUFU ex2 and a cubic on the FMA pipe so both pipes work.  The
+//    running max m is raised lazily (only when a tile's max exceeds it by a
+//    threshold, the idea of the reference's ``rowmax > m + 8`` at :267); with
+//    f16 P the threshold is wide and m is speculative: P is computed with the
+//    old m while the tile max is taken, and recomputed only in the rare tile
+//    that raises m, after the softmax warp has rescaled its rows of O in TMEM.
 //  * every mbarrier wait is bounded; a timeout sets an error word and lets the
 //    CTA run to teardown (TMEM is always freed, copies in flight drained).
 #include <mutex>
 #include <string>
+#include <type_traits>
 
 #include "mh3_b200.h"
 #include "mh3_internal.h"
@@ -40,8 +44,22 @@ constexpr int BN = 128;  // keys per K/V tile
 constexpr int KST = 3;   // K ring depth
 constexpr int VST = 3;   // V ring depth
 constexpr int NUM_THREADS = 384;
-constexpr float LAZY_T = 4.5f;    // lazy max threshold (log2 units)
-constexpr float P_OFFSET = 4.0f;  // P = 2^(x + P_OFFSET) <= 2^(LAZY_T+P_OFFSET) < 448
+// Lazy max threshold and P offset (log2 units), P = 2^(x - m + offset):
+//  e4m3 P: P <= 2^(4 + 4.5) < 448, and the row max lands on 2^4 (exact);
+//  f16 P:  P <= 2^12, far inside f16; the wide threshold makes the running
+//          max rise in very few tiles, so its speculative P rarely reruns.
+constexpr float LAZY_T8 = 4.5f;
+constexpr float P_OFFSET8 = 4.0f;
+constexpr float LAZY_T16 = 12.0f;
+constexpr float P_OFFSET16 = 0.0f;
+#ifndef MH3_POLY_PAIRS
+#define MH3_POLY_PAIRS 0
+#endif
+#ifndef MH3_MUFU_F16X2
+#define MH3_MUFU_F16X2 0
+#endif
+// of every 8 exp2 pairs, how many run on the FMA pipe (the rest on MUFU)
+constexpr int kPolyPairs = MH3_POLY_PAIRS;
 
 struct Params {
   CUtensorMap tmq;  // e4m3 (D, S, H, B), box (D, 128, 1, 1)
@@ -274,8 +292,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
     const float* skp = p.sk + b * p.skb + h * p.skh;
     const float* biasp = HAS_BIAS ? (p.kbias2 + b * p.kbias_sb) : nullptr;
 
-    float m = -1.0e30f;  // running max (log2 units), raised lazily
-    float l = 0.0f;      // running sum of 2^(x + P_OFFSET)
+    // Running max m (log2 units); -2^20 stands for "no key yet" (finite, so
+    // that the FMA-pipe exp2's clamp bound stays exact to well under 1).
+    float m = -1048576.0f;
+    float l = 0.0f;  // running sum of P
     for (int j = 0; j < nk; ++j) {
       mbar_wait(smem_u32(&sm.bar_s[t]), (uint32_t)j & 1u, g);
       tc_fence_after();
@@ -285,94 +305,155 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
       tmem_wait_ld();
 
       const float c_tile = cq * __ldg(skp + (long long)j * p.skblk);
-      float tmax;
-      float2 cc;
-      if constexpr (HAS_BIAS) {
-        // t = s*c + bias2 (bias2 = -inf for masked or padding keys)
-        const float4* bp = reinterpret_cast<const float4*>(biasp + (long long)j * BN);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
+      const int rem = k_len - j * BN;
+      // Raw S chunk c (32 keys) -> the value P is taken from: s*c + bias2 with
+      // bias2 = -inf for masked or padding keys (HAS_BIAS), else s with the
+      // keys past the end of the sequence set to -inf.
+      auto prep = [&](int c) {
+        if constexpr (HAS_BIAS) {
+          const float4* bp = reinterpret_cast<const float4*>(biasp + (long long)j * BN) + c * 8;
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            const float4 bb = __ldg(bp + c * 8 + i);
+            const float4 bb = __ldg(bp + i);
             sr[c][4 * i + 0] = f2u(fmaf(u2f(sr[c][4 * i + 0]), c_tile, bb.x));
             sr[c][4 * i + 1] = f2u(fmaf(u2f(sr[c][4 * i + 1]), c_tile, bb.y));
             sr[c][4 * i + 2] = f2u(fmaf(u2f(sr[c][4 * i + 2]), c_tile, bb.z));
             sr[c][4 * i + 3] = f2u(fmaf(u2f(sr[c][4 * i + 3]), c_tile, bb.w));
           }
-        }
-        cc = make_float2(1.0f, 1.0f);
-      } else {
-        const int rem = k_len - j * BN;
-        if (rem < BN) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
+        } else {
+          if (rem < BN) {
 #pragma unroll
             for (int i = 0; i < 32; ++i)
               if (c * 32 + i >= rem) sr[c][i] = f2u(-INFINITY);
-        }
-        cc = make_float2(c_tile, c_tile);
-      }
-      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        mx0 = fmax3(mx0, u2f(sr[0][i]), u2f(sr[0][i + 1]));
-        mx1 = fmax3(mx1, u2f(sr[1][i]), u2f(sr[1][i + 1]));
-        mx2 = fmax3(mx2, u2f(sr[2][i]), u2f(sr[2][i + 1]));
-        mx3 = fmax3(mx3, u2f(sr[3][i]), u2f(sr[3][i + 1]));
-      }
-      float rmax = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-      tmax = HAS_BIAS ? rmax : rmax * c_tile;
-
-      const bool upd = tmax > m + LAZY_T;
-      const float m_new = upd ? tmax : m;
-      const float alpha = ex2_approx(m - m_new);  // 1 when not raised, 0 from the initial sentinel
-      if (j > 0 && __any_sync(0xffffffffu, upd)) {
-        // Rescale this row of O in TMEM.  PV(j-1) has completed: the commit
-        // behind bar_s(j) tracks every MMA issued before S(j).
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + (uint32_t)(c * 32), o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = f2u(u2f(o[i]) * alpha);
-          tmem_st32(tO + (uint32_t)(c * 32), o);
-        }
-      }
-      l *= alpha;
-      m = m_new;
-
-      const float nb = P_OFFSET - m;
-      const float2 nn = make_float2(nb, nb);
-      float lsum = 0.0f;
-      // P for 32 keys at a time: f16 pairs (PV16, 16 columns) or e4m3
-      // quads (8 columns), stored over the first columns of S.
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t hacc = 0u;
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float2 x = ffma2(make_float2(u2f(sr[c][2 * i]), u2f(sr[c][2 * i + 1])), cc, nn);
-          const uint32_t e = ex2_f16x2(cvt_f16x2(x.y, x.x));
-          hacc = hadd2(hacc, e);
-          if constexpr (PV16) {
-            pk[i] = e;
-          } else {
-            const uint32_t p2 = cvt_e4m3x2_f16x2(e);
-            if (i & 1)
-              pk[i >> 1] |= p2 << 16;
-            else
-              pk[i >> 1] = p2;
           }
         }
-        const float2 hs = f16x2_to_float2(hacc);
-        lsum += hs.x + hs.y;
-        if constexpr (PV16)
-          tmem_st16(tS + (uint32_t)(c * 16), pk);
-        else
-          tmem_st8(tS + (uint32_t)(c * 8), pk);
+      };
+#pragma unroll
+      for (int c = 0; c < 4; ++c) prep(c);
+      const float2 cc = HAS_BIAS ? make_float2(1.0f, 1.0f) : make_float2(c_tile, c_tile);
+      const float inv_c = HAS_BIAS ? 1.0f : __frcp_rn(c_tile);
+
+      // P for the 128 keys of this tile from the S values in registers, stored
+      // over the first columns of S as f16 pairs (PV16, 16 columns per 32
+      // keys) or e4m3 quads (8 columns); returns the row sum (f32, of the
+      // unrounded values).  Of the 8 pairs in each 16-key group the first
+      // kPolyPairs take the FMA-pipe exp2 and the rest MUFU ex2, so both
+      // pipes work at once.  With TRACK the tile max of s is folded in on the
+      // way (speculative pass).
+      auto p_pass = [&](float nb, auto track, float& smax) -> float {
+        constexpr bool TRACK = decltype(track)::value;
+        const float2 nn = make_float2(nb, nb);
+        // FMA-pipe form: 2^(s*c + nb) = 2^(s*c + floor(nb)) * 2^frac(nb).
+        const float nbi = floorf(nb);
+        const Exp2Coef kc = exp2_coef(ex2_approx(nb - nbi));
+        const float2 nbm = make_float2(nbi + kRoundMagic, nbi + kRoundMagic);
+        const float lo = (-126.0f - nbi) * inv_c;  // s >= lo  <=>  s*c + floor(nb) >= -126
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        float2 lsum2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int gg = 0; gg < 8; ++gg) {  // 16 keys per group, keys 64..127 first
+          const int g = (gg + 4) & 7;
+          const int c = g >> 1, i0 = (g & 1) * 8;
+          uint32_t pk[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float s0 = u2f(sr[c][2 * (i0 + i)]), s1 = u2f(sr[c][2 * (i0 + i) + 1]);
+            if constexpr (TRACK) mx[c] = fmax3(mx[c], s0, s1);
+            float2 pp;
+            uint32_t e = 0u;
+            if (i < kPolyPairs) {
+              pp = exp2_fma_pipe(make_float2(fmaxf(s0, lo), fmaxf(s1, lo)), cc, nbm, kc);
+            } else {
+              const float2 x = ffma2(make_float2(s0, s1), cc, nn);
+              if constexpr (MH3_MUFU_F16X2 && PV16) {
+                e = ex2_f16x2(cvt_f16x2(x.y, x.x));
+                pp = f16x2_to_float2(e);
+              } else {
+                pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+              }
+            }
+            lsum2 = __fadd2_rn(lsum2, pp);
+            (void)e;
+            if constexpr (PV16) {
+              pk[i] = (MH3_MUFU_F16X2 && i >= kPolyPairs) ? e : cvt_f16x2(pp.y, pp.x);
+            } else {
+              const uint32_t p2 = cvt_e4m3x2_f32(pp.y, pp.x);
+              if (i & 1)
+                pk[i >> 1] |= p2 << 16;
+              else
+                pk[i >> 1] = p2;
+            }
+          }
+          if constexpr (PV16)
+            tmem_st8(tS + (uint32_t)(g * 8), pk);
+          else
+            tmem_st4(tS + (uint32_t)(g * 4), pk);
+        }
+        if constexpr (TRACK) smax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        return lsum2.x + lsum2.y;
+      };
+      auto to_logit = [&](float sm) { return HAS_BIAS ? sm : sm * c_tile; };
+      // Rescale this row of O in TMEM.  PV(j-1) has completed: the commit
+      // behind bar_s(j) tracks every MMA issued before S(j).
+      auto rescale_o = [&](float alpha) {
+#pragma unroll
+        for (int c = 0; c < D / 16; ++c) {
+          uint32_t o[16];
+          tmem_ld16(tO + (uint32_t)(c * 16), o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = f2u(u2f(o[i]) * alpha);
+          tmem_st16(tO + (uint32_t)(c * 16), o);
+        }
+      };
+      using kTrack = std::integral_constant<bool, true>;
+      using kNoTrack = std::integral_constant<bool, false>;
+      constexpr float kLazy = PV16 ? LAZY_T16 : LAZY_T8;
+      constexpr float kOffset = PV16 ? P_OFFSET16 : P_OFFSET8;
+
+      float lsum;
+      float smax = -INFINITY;
+      if (!PV16 || j == 0) {
+        // Tile max first, then P.
+        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          mx0 = fmax3(mx0, u2f(sr[0][i]), u2f(sr[0][i + 1]));
+          mx1 = fmax3(mx1, u2f(sr[1][i]), u2f(sr[1][i + 1]));
+          mx2 = fmax3(mx2, u2f(sr[2][i]), u2f(sr[2][i + 1]));
+          mx3 = fmax3(mx3, u2f(sr[3][i]), u2f(sr[3][i + 1]));
+        }
+        const float tmax = to_logit(fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)));
+        const bool upd = tmax > m + kLazy;
+        const float m_new = upd ? tmax : m;
+        const float alpha = ex2_approx(m - m_new);  // 1 when kept, 0 from the sentinel
+        if (j > 0 && __any_sync(0xffffffffu, upd)) rescale_o(alpha);
+        l *= alpha;
+        m = m_new;
+        lsum = p_pass(kOffset - m, kNoTrack{}, smax);
+      } else {
+        // f16 P: speculate that m stands, compute P and the tile max together,
+        // and redo P only when some row of the warp has to raise m.
+        lsum = p_pass(kOffset - m, kTrack{}, smax);
+        const float tmax = to_logit(smax);
+        const bool upd = tmax > m + kLazy;
+        if (__any_sync(0xffffffffu, upd)) {
+          const float m_new = upd ? tmax : m;
+          const float alpha = ex2_approx(m - m_new);  // 1 for rows that keep m
+          rescale_o(alpha);
+          l *= alpha;
+          m = m_new;
+          // P (64 columns of f16) overwrote S of keys 0..63 only, which are
+          // still in registers; S of keys 64..127 is read again from TMEM so
+          // that its registers could be released early.
+          tmem_ld32(tS + 64u, sr[2]);
+          tmem_ld32(tS + 96u, sr[3]);
+          tmem_wait_ld();
+          prep(2);
+          prep(3);
+          tmem_wait_st();  // the speculative P stores land before they are overwritten
+          lsum = p_pass(kOffset - m, kNoTrack{}, smax);
+        }
       }
       l += lsum;
       tmem_wait_st();

@@ -186,7 +186,17 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
-// 32 lanes x 16 / 8 consecutive 32-bit columns (stores).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15])
+      : "r"(taddr));
+}
+
+// 32 lanes x 16 / 8 / 4 consecutive 32-bit columns (stores).
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
@@ -199,6 +209,12 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
                "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t* r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3])
                : "memory");
 }
 
@@ -375,6 +391,44 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
   float2 d;
   asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(ud));
   return d;
+}
+
+// Cubic minimax fit of 2^f on [0, 1] (Remez; max relative error 7.5e-5,
+// i.e. finer than the f16 rounding of P that follows).
+constexpr float kExp2C0 = 0.9999251961708069f;
+constexpr float kExp2C1 = 0.6958336234092712f;
+constexpr float kExp2C2 = 0.22606725990772247f;
+constexpr float kExp2C3 = 0.07802427560091019f;
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+
+// 2^(s*c + nb) * w for a pair on the FMA pipe instead of MUFU.  The caller
+// folds the weight w into the Horner coefficients (k[i] = kExp2C<i> * w,
+// w in [1, 2), e.g. 2^frac(nb') for a non-integral offset nb').  Requirements:
+// nb is an integer with |nb| < 2^21, nbm = nb + kRoundMagic, and
+// s*c + nb >= -126 (so the exponent field below stays >= 0).
+//   t = RD(s*c + nbm)   -> low mantissa bits of t hold n = floor(s*c + nb)
+//   d = nbm - t = nb - n (exact: both are integers in [2^23, 2^24))
+//   f = s*c + d in [0, 1],  w*2^f by Horner,  2^n by adding n to the exponent.
+struct Exp2Coef {
+  float2 k0, k1, k2, k3;
+};
+
+__device__ __forceinline__ Exp2Coef exp2_coef(float w) {
+  return {make_float2(kExp2C0 * w, kExp2C0 * w), make_float2(kExp2C1 * w, kExp2C1 * w),
+          make_float2(kExp2C2 * w, kExp2C2 * w), make_float2(kExp2C3 * w, kExp2C3 * w)};
+}
+
+__device__ __forceinline__ float2 exp2_fma_pipe(float2 s, float2 c, float2 nbm, const Exp2Coef& k) {
+  const float2 t = __ffma2_rd(s, c, nbm);
+  const float2 d = __ffma2_rn(t, make_float2(-1.0f, -1.0f), nbm);
+  const float2 f = __ffma2_rn(s, c, d);
+  float2 q = __ffma2_rn(k.k3, f, k.k2);
+  q = __ffma2_rn(q, f, k.k1);
+  q = __ffma2_rn(q, f, k.k0);
+  // (bits(t) << 23) == n << 23 (mod 2^32): the magic's own bits shift out.
+  const uint32_t ex = (__float_as_uint(t.x) << 23) + __float_as_uint(q.x);
+  const uint32_t ey = (__float_as_uint(t.y) << 23) + __float_as_uint(q.y);
+  return make_float2(__uint_as_float(ex), __uint_as_float(ey));
 }
 
 }  // namespace mh3

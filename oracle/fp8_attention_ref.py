@@ -270,6 +270,19 @@ def sdpa_dequant_oracle(
 # LAZY_T, and P = 2^(s - m + P_OFFSET) stays <= 2^(LAZY_T + P_OFFSET) < 448.
 LAZY_T = 4.5
 P_OFFSET = 4.0
+LAZY_T16 = 12.0
+P_OFFSET16 = 0.0
+
+
+def softmax_params(p_dtype: torch.dtype) -> tuple[float, float]:
+    """(lazy threshold, P offset) the kernel uses for a P dtype (log2 units).
+
+    e4m3 P: P <= 2^(4 + 4.5) < 448 with the row max at exactly 2^4; 16-bit
+    P: a wide threshold (P <= 2^12) so that the running max rises in few tiles.
+    """
+    if p_dtype == E4M3:
+        return LAZY_T, P_OFFSET
+    return LAZY_T16, P_OFFSET16
 
 
 def exp2_attention_emulation(
@@ -283,8 +296,8 @@ def exp2_attention_emulation(
     key_mask: torch.Tensor | None = None,
     key_bias: torch.Tensor | None = None,
     block_n: int = 128,
-    lazy_t: float = LAZY_T,
-    p_offset: float = P_OFFSET,
+    lazy_t: float | None = None,
+    p_offset: float | None = None,
     p_dtype: torch.dtype = E4M3,
 ) -> torch.Tensor:
     """Block algorithm of the CUDA kernel with exact exp2 (float32 result).
@@ -293,11 +306,15 @@ def exp2_attention_emulation(
     the tile max exceeds it by ``lazy_t``; ``P = e4m3(2^(t - m + p_offset))``
     feeds the PV product (``p_dtype`` = torch.bfloat16 / float16 for the
     kernel's 16-bit-PV variant); the row sum uses the unrounded 2^(...)
-    values.
+    values.  ``lazy_t`` / ``p_offset`` default to the kernel's values for
+    ``p_dtype`` (``softmax_params``).
     Scales: scale_q/scale_k per 128-row block [B,H,nblk] (broadcast a
     per-(b,h) scale by passing nblk=1), scale_v per channel [B,H,D] (or
     [B,H,1]).
     """
+    d_lazy, d_off = softmax_params(p_dtype)
+    lazy_t = d_lazy if lazy_t is None else lazy_t
+    p_offset = d_off if p_offset is None else p_offset
     B, H, Sq, D = q8.shape
     Sk = k8.shape[2]
     nk = cdiv(Sk, block_n)

@@ -188,6 +188,42 @@ def test_attention_strided_views(pv):
 
 
 @pytest.mark.parametrize("pv", ["f16", "e4m3"])
+@pytest.mark.parametrize("use_bias", [False, True])
+def test_attention_rising_row_max(pv, use_bias):
+    """Logits that grow along the keys raise the running max in most tiles.
+
+    The kernel computes P with the old max while it takes the tile max and
+    redoes the tile when a row has to raise it; this drives that path (and
+    the O rescale) on nearly every tile, through the scale and bias forms.
+    """
+    from minimaxh3_b200 import ops
+
+    B, H, Sq, Sk, D = 1, 2, 256, 2000, 128
+    g = torch.Generator().manual_seed(21)
+    u = torch.randn(D, generator=g)
+    u = u / u.norm()
+    ramp = torch.linspace(0.0, 1.0, Sk)
+    q = 3.0 * u + 0.5 * torch.randn(B, H, Sq, D, generator=g)
+    if use_bias:
+        k = torch.randn(B, H, Sk, D, generator=g)
+        key_bias = (80.0 * ramp)[None].expand(B, Sk).contiguous()
+    else:
+        k = (300.0 * ramp)[:, None] * u + 0.5 * torch.randn(B, H, Sk, D, generator=g)
+        key_bias = None
+    v = torch.randn(B, H, Sk, D, generator=g)
+    (q8, sq), (k8, sk), (v8, sv) = (_per_bh(t.to(torch.bfloat16)) for t in (q, k, v))
+    ls2 = OA.LOG2E / math.sqrt(D)
+    kw = {}
+    if use_bias:
+        kw["key_bias2"] = ops.build_key_bias2(None, key_bias.to(DEV), B, Sk, DEV)
+    out = _run_e4m3(q8, k8, v8, sq[..., None], sk[..., None], sv[..., None], ls2, pv=pv, **kw).float().cpu()
+    assert torch.isfinite(out).all()
+    ref = OA.sdpa_dequant_oracle(q8.double() * sq[..., None, None], k8.double() * sk[..., None, None],
+                                 v8.double() * sv[..., None, None], ls2, key_bias=key_bias, base2=True)
+    _check(OA.compare(out, ref), pv)
+
+
+@pytest.mark.parametrize("pv", ["f16", "e4m3"])
 def test_attention_large_head_subset_property(pv):
     """Config-2 sequence length: finite, and sampled rows match the oracle."""
     B, H, S, D = 1, 2, 32760, 128
