@@ -47,6 +47,13 @@ B, H, S, D = 1, 40, 32760, 128
 NOMINAL_FP8_TFLOPS = 4500.0
 
 
+# DRAM bytes (read + write) of one config-2 attention launch from the ncu
+# capture summarised in profiles/attn_fwd_config2.md: H=8 measured
+# (134.5 MB read + 41.3 MB write), scaled to H=40 by the heads processed
+# (each (batch, head) is an independent set of CTAs reading its own Q, K, V).
+ATTN_TRAFFIC_BYTES_H40 = {"f16": 5 * (134.476e6 + 41.250e6)}
+
+
 def _peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -425,7 +432,14 @@ def run_gpu_arm(args, dist, rank, world, local):
         "pct_of_fp8_peak": achieved / peaks["fp8_tflops"],
         "pct_of_nominal_fp8_peak": achieved / NOMINAL_FP8_TFLOPS,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["fp8_tflops"], "unit": "TFLOP/s",
-                     "frac": achieved / peaks["fp8_tflops"], "traffic": None, "peak_source": peaks["source"],
+                     "frac": achieved / peaks["fp8_tflops"],
+                     "traffic": ATTN_TRAFFIC_BYTES_H40.get(args.pv) if H == 40 else None,
+                     "traffic_source": "ncu dram__bytes_read+write, H=8 capture x5 (profiles/attn_fwd_config2.md)",
+                     "peak_source": peaks["source"],
+                     # half the FLOPs (PV) run at the 16-bit rate with f16 P/V:
+                     # the attainable peak is the harmonic mix of the two rates
+                     "peak_mixed": (1.0 / (0.5 / peaks["fp8_tflops"] + 0.5 / (peaks["fp8_tflops"] / 2))
+                                    if args.pv == "f16" else peaks["fp8_tflops"]),
                      "kernel": "mh3::attn::fwd_kernel", "avg_launch_ms": avg_launch_ms},
         "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "minimaxh3_b200.kernels.fp8_attention.fp8_attention (bf16 in/out, quantise + attention)",

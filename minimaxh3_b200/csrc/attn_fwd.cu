@@ -12,20 +12,21 @@
 //      warp  9     tcgen05 MMA issuer; owns the 512-column TMEM allocation
 //      warps 10-11 idle (complete the third warpgroup for setmaxnreg)
 //  * TMEM columns: S0 [0,128)  S1 [128,256)  O0 [256,256+D)  O1 [256+D,256+2D);
-//    P (128x128 e4m3 = 32 columns) is written over the first 32 columns of S.
-//  * S = Q K^T and O += P V are tcgen05.mma kind::f8f6f4 (M=128, K=32 steps).
-//    V stays in its natural [key, channel] layout: the PV MMA reads it as an
-//    MN-major B operand, so no transposed copy of V is ever made.
-//  * MMA order  S0(0) S1(0) | PV0(j) S0(j+1) PV1(j) S1(j+1) ... : the tensor
-//    core works on one Q tile while the other tile's softmax runs.
-//  * softmax: exp2 with the dequant scales folded into one FMA per element,
-//    P = 2^(s*c - m + offset) as f16 (or e4m3); the exp2 pairs are split
-//    between MUFU ex2 and a cubic on the FMA pipe so both pipes work.  The
-//    running max m is raised lazily (only when a tile's max exceeds it by a
-//    threshold, the idea of the reference's ``rowmax > m + 8`` at :267); with
-//    f16 P the threshold is wide and m is speculative: P is computed with the
-//    old m while the tile max is taken, and recomputed only in the rare tile
-//    that raises m, after the softmax warp has rescaled its rows of O in TMEM.
+//    P (f16: 64 columns, e4m3: 32) is written over the first columns of S.
+//  * S = Q K^T is tcgen05.mma kind::f8f6f4; O += P V is kind::f16 with f16 P
+//    and V (default) or kind::f8f6f4 with e4m3 P and V.  V stays in its
+//    natural [key, channel] layout: the PV MMA reads it as an MN-major B
+//    operand, so no transposed copy of V is ever made.
+//  * MMA order per Q tile t and KV step j: as soon as the softmax has read
+//    S(t, j) into registers, S(t, j+1) for keys 64..127 (columns 64..127,
+//    which P never touches) is issued; after P(t, j): PV(t, j), then
+//    S(t, j+1) for keys 0..63.  The two Q tiles alternate, so the tensor core
+//    works on one tile while the other tile's softmax runs.
+//  * softmax (one thread per row): tile max, lazy running max (raised only
+//    when a tile's max exceeds it by a threshold, the idea of the reference's
+//    ``rowmax > m + 8`` at :267; the rare raise rescales the row of O in TMEM),
+//    then P = 2^(s*c - m + offset) with the dequant scales folded into one
+//    packed FMA per pair and two f32 MUFU ex2.
 //  * every mbarrier wait is bounded; a timeout sets an error word and lets the
 //    CTA run to teardown (TMEM is always freed, copies in flight drained).
 #include <mutex>
@@ -47,19 +48,11 @@ constexpr int NUM_THREADS = 384;
 // Lazy max threshold and P offset (log2 units), P = 2^(x - m + offset):
 //  e4m3 P: P <= 2^(4 + 4.5) < 448, and the row max lands on 2^4 (exact);
 //  f16 P:  P <= 2^12, far inside f16; the wide threshold makes the running
-//          max rise in very few tiles, so its speculative P rarely reruns.
+//          max (and the O rescale) rise in very few tiles.
 constexpr float LAZY_T8 = 4.5f;
 constexpr float P_OFFSET8 = 4.0f;
 constexpr float LAZY_T16 = 12.0f;
 constexpr float P_OFFSET16 = 0.0f;
-#ifndef MH3_POLY_PAIRS
-#define MH3_POLY_PAIRS 0
-#endif
-#ifndef MH3_MUFU_F16X2
-#define MH3_MUFU_F16X2 0
-#endif
-// of every 8 exp2 pairs, how many run on the FMA pipe (the rest on MUFU)
-constexpr int kPolyPairs = MH3_POLY_PAIRS;
 
 struct Params {
   CUtensorMap tmq;  // e4m3 (D, S, H, B), box (D, 128, 1, 1)
@@ -94,6 +87,7 @@ struct __align__(1024) Smem {
   uint64_t bar_vfull[VST];
   uint64_t bar_vempty[VST];
   uint64_t bar_s[2];
+  uint64_t bar_sld[2];  // softmax has read S(j) into registers
   uint64_t bar_p[2];
   uint64_t bar_o;
   uint32_t tmem_base;
@@ -150,6 +144,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&sm.bar_s[i]), 1);
+      mbar_init(smem_u32(&sm.bar_sld[i]), 4);
       mbar_init(smem_u32(&sm.bar_p[i]), 4);
     }
     mbar_init(smem_u32(&sm.bar_o), 1);
@@ -213,6 +208,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
     } else if (warp == 9 && lane == 0) {
       // ---------------------------------------------------------------- MMA issuer
       constexpr uint32_t kIdescS = idesc_e4m3(BM, BN, false, false);
+      constexpr uint32_t kIdescS64 = idesc_e4m3(BM, BN / 2, false, false);
       constexpr uint32_t kIdescO = PV16 ? idesc_f16(BM, D, false, true) : idesc_e4m3(BM, D, false, true);
       const uint32_t tS[2] = {tmem + 0u, tmem + 128u};
       const uint32_t tO[2] = {tmem + 256u, tmem + 256u + (uint32_t)D};
@@ -232,6 +228,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
 #pragma unroll
         for (int kk = 0; kk < D / 32; ++kk) mma_f8_ss(tS[t], kmaj(q_base[t], kk), kmaj(kb, kk), kIdescS, kk > 0);
       };
+      // Half of S(t, j+1): keys [half*64, half*64+64) into S columns
+      // [half*64, half*64+64) (N = 64; K rows 64.. start on a swizzle atom).
+      auto issue_s_half = [&](int t, int ks, int half) {
+        const uint32_t kb = smem_u32(sm.k[ks]) + (uint32_t)(half * (BN / 2) * kRowBytes);
+#pragma unroll
+        for (int kk = 0; kk < D / 32; ++kk)
+          mma_f8_ss(tS[t] + (uint32_t)(half * (BN / 2)), kmaj(q_base[t], kk), kmaj(kb, kk), kIdescS64, kk > 0);
+      };
       bool ok = mbar_wait(smem_u32(&sm.bar_q), 0, g);
       if (nk > 0) {
         ok = mbar_wait(smem_u32(&sm.bar_kfull[0]), 0, g) && ok;
@@ -242,12 +246,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
         mma_commit(smem_u32(&sm.bar_s[1]));
         mma_commit(smem_u32(&sm.bar_kempty[0]));
       }
+      // Per tile t and step j: S(t, j+1) keys 64..127 go into S columns
+      // 64..127 as soon as the softmax has read S(t, j) (P only overwrites
+      // columns 0..63); PV(t, j) then S(t, j+1) keys 0..63 follow P(t, j).
       for (int j = 0; j < nk; ++j) {
         const int vs = j % VST;
         mbar_wait(smem_u32(&sm.bar_vfull[vs]), (uint32_t)(j / VST) & 1u, g);
         const int ks = (j + 1) % KST;
+        const bool has_next = j + 1 < nk;
+        if (has_next) mbar_wait(smem_u32(&sm.bar_kfull[ks]), (uint32_t)((j + 1) / KST) & 1u, g);
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
+          if (has_next) {
+            mbar_wait(smem_u32(&sm.bar_sld[t]), (uint32_t)j & 1u, g);
+            tc_fence_after();
+            issue_s_half(t, ks, 1);
+          }
           mbar_wait(smem_u32(&sm.bar_p[t]), (uint32_t)j & 1u, g);
           tc_fence_after();
           if constexpr (PV16) {
@@ -260,12 +274,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
               mma_f8_ts(tO[t], tS[t] + (uint32_t)(kk * 8), vdesc(vs, kk), kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
           }
           if (t == 1) mma_commit(smem_u32(&sm.bar_vempty[vs]));
-          if (j + 1 < nk) {
-            if (t == 0) {
-              mbar_wait(smem_u32(&sm.bar_kfull[ks]), (uint32_t)((j + 1) / KST) & 1u, g);
-              tc_fence_after();
-            }
-            issue_s(t, ks);
+          if (has_next) {
+            issue_s_half(t, ks, 0);
             mma_commit(smem_u32(&sm.bar_s[t]));
             if (t == 1) mma_commit(smem_u32(&sm.bar_kempty[ks]));
           }
@@ -292,9 +302,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
     const float* skp = p.sk + b * p.skb + h * p.skh;
     const float* biasp = HAS_BIAS ? (p.kbias2 + b * p.kbias_sb) : nullptr;
 
-    // Running max m (log2 units); -2^20 stands for "no key yet" (finite, so
-    // that the FMA-pipe exp2's clamp bound stays exact to well under 1).
-    float m = -1048576.0f;
+    float m = -1.0e30f;  // running max (log2 units), raised lazily; -1e30 = no key yet
     float l = 0.0f;  // running sum of P
     for (int j = 0; j < nk; ++j) {
       mbar_wait(smem_u32(&sm.bar_s[t]), (uint32_t)j & 1u, g);
@@ -303,6 +311,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(tS + (uint32_t)(c * 32), sr[c]);
       tmem_wait_ld();
+      // S(j) is in registers: S columns 64..127 may take the next S.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sm.bar_sld[t]));
 
       const float c_tile = cq * __ldg(skp + (long long)j * p.skblk);
       const int rem = k_len - j * BN;
@@ -331,71 +343,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
 #pragma unroll
       for (int c = 0; c < 4; ++c) prep(c);
       const float2 cc = HAS_BIAS ? make_float2(1.0f, 1.0f) : make_float2(c_tile, c_tile);
-      const float inv_c = HAS_BIAS ? 1.0f : __frcp_rn(c_tile);
+      constexpr float kLazy = PV16 ? LAZY_T16 : LAZY_T8;
+      constexpr float kOffset = PV16 ? P_OFFSET16 : P_OFFSET8;
 
-      // P for the 128 keys of this tile from the S values in registers, stored
-      // over the first columns of S as f16 pairs (PV16, 16 columns per 32
-      // keys) or e4m3 quads (8 columns); returns the row sum (f32, of the
-      // unrounded values).  Of the 8 pairs in each 16-key group the first
-      // kPolyPairs take the FMA-pipe exp2 and the rest MUFU ex2, so both
-      // pipes work at once.  With TRACK the tile max of s is folded in on the
-      // way (speculative pass).
-      auto p_pass = [&](float nb, auto track, float& smax) -> float {
-        constexpr bool TRACK = decltype(track)::value;
-        const float2 nn = make_float2(nb, nb);
-        // FMA-pipe form: 2^(s*c + nb) = 2^(s*c + floor(nb)) * 2^frac(nb).
-        const float nbi = floorf(nb);
-        const Exp2Coef kc = exp2_coef(ex2_approx(nb - nbi));
-        const float2 nbm = make_float2(nbi + kRoundMagic, nbi + kRoundMagic);
-        const float lo = (-126.0f - nbi) * inv_c;  // s >= lo  <=>  s*c + floor(nb) >= -126
-        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        float2 lsum2 = make_float2(0.0f, 0.0f);
+      // Tile max; raise the running max lazily and rescale this row of O in
+      // TMEM on the rare raise (PV(j-1) has completed: the commit behind
+      // bar_s(j) tracks every MMA issued before S(j)).
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-        for (int gg = 0; gg < 8; ++gg) {  // 16 keys per group, keys 64..127 first
-          const int g = (gg + 4) & 7;
-          const int c = g >> 1, i0 = (g & 1) * 8;
-          uint32_t pk[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float s0 = u2f(sr[c][2 * (i0 + i)]), s1 = u2f(sr[c][2 * (i0 + i) + 1]);
-            if constexpr (TRACK) mx[c] = fmax3(mx[c], s0, s1);
-            float2 pp;
-            uint32_t e = 0u;
-            if (i < kPolyPairs) {
-              pp = exp2_fma_pipe(make_float2(fmaxf(s0, lo), fmaxf(s1, lo)), cc, nbm, kc);
-            } else {
-              const float2 x = ffma2(make_float2(s0, s1), cc, nn);
-              if constexpr (MH3_MUFU_F16X2 && PV16) {
-                e = ex2_f16x2(cvt_f16x2(x.y, x.x));
-                pp = f16x2_to_float2(e);
-              } else {
-                pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-              }
-            }
-            lsum2 = __fadd2_rn(lsum2, pp);
-            (void)e;
-            if constexpr (PV16) {
-              pk[i] = (MH3_MUFU_F16X2 && i >= kPolyPairs) ? e : cvt_f16x2(pp.y, pp.x);
-            } else {
-              const uint32_t p2 = cvt_e4m3x2_f32(pp.y, pp.x);
-              if (i & 1)
-                pk[i >> 1] |= p2 << 16;
-              else
-                pk[i >> 1] = p2;
-            }
-          }
-          if constexpr (PV16)
-            tmem_st8(tS + (uint32_t)(g * 8), pk);
-          else
-            tmem_st4(tS + (uint32_t)(g * 4), pk);
-        }
-        if constexpr (TRACK) smax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-        return lsum2.x + lsum2.y;
-      };
-      auto to_logit = [&](float sm) { return HAS_BIAS ? sm : sm * c_tile; };
-      // Rescale this row of O in TMEM.  PV(j-1) has completed: the commit
-      // behind bar_s(j) tracks every MMA issued before S(j).
-      auto rescale_o = [&](float alpha) {
+      for (int i = 0; i < 32; i += 2) {
+        mx0 = fmax3(mx0, u2f(sr[0][i]), u2f(sr[0][i + 1]));
+        mx1 = fmax3(mx1, u2f(sr[1][i]), u2f(sr[1][i + 1]));
+        mx2 = fmax3(mx2, u2f(sr[2][i]), u2f(sr[2][i + 1]));
+        mx3 = fmax3(mx3, u2f(sr[3][i]), u2f(sr[3][i + 1]));
+      }
+      const float rmax = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      const float tmax = HAS_BIAS ? rmax : rmax * c_tile;
+      const bool upd = tmax > m + kLazy;
+      const float m_new = upd ? tmax : m;
+      const float alpha = ex2_approx(m - m_new);  // 1 when kept, 0 from the sentinel
+      if (j > 0 && __any_sync(0xffffffffu, upd)) {
 #pragma unroll
         for (int c = 0; c < D / 16; ++c) {
           uint32_t o[16];
@@ -405,56 +372,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
           for (int i = 0; i < 16; ++i) o[i] = f2u(u2f(o[i]) * alpha);
           tmem_st16(tO + (uint32_t)(c * 16), o);
         }
-      };
-      using kTrack = std::integral_constant<bool, true>;
-      using kNoTrack = std::integral_constant<bool, false>;
-      constexpr float kLazy = PV16 ? LAZY_T16 : LAZY_T8;
-      constexpr float kOffset = PV16 ? P_OFFSET16 : P_OFFSET8;
-
-      float lsum;
-      float smax = -INFINITY;
-      if (!PV16 || j == 0) {
-        // Tile max first, then P.
-        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          mx0 = fmax3(mx0, u2f(sr[0][i]), u2f(sr[0][i + 1]));
-          mx1 = fmax3(mx1, u2f(sr[1][i]), u2f(sr[1][i + 1]));
-          mx2 = fmax3(mx2, u2f(sr[2][i]), u2f(sr[2][i + 1]));
-          mx3 = fmax3(mx3, u2f(sr[3][i]), u2f(sr[3][i + 1]));
-        }
-        const float tmax = to_logit(fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)));
-        const bool upd = tmax > m + kLazy;
-        const float m_new = upd ? tmax : m;
-        const float alpha = ex2_approx(m - m_new);  // 1 when kept, 0 from the sentinel
-        if (j > 0 && __any_sync(0xffffffffu, upd)) rescale_o(alpha);
-        l *= alpha;
-        m = m_new;
-        lsum = p_pass(kOffset - m, kNoTrack{}, smax);
-      } else {
-        // f16 P: speculate that m stands, compute P and the tile max together,
-        // and redo P only when some row of the warp has to raise m.
-        lsum = p_pass(kOffset - m, kTrack{}, smax);
-        const float tmax = to_logit(smax);
-        const bool upd = tmax > m + kLazy;
-        if (__any_sync(0xffffffffu, upd)) {
-          const float m_new = upd ? tmax : m;
-          const float alpha = ex2_approx(m - m_new);  // 1 for rows that keep m
-          rescale_o(alpha);
-          l *= alpha;
-          m = m_new;
-          // P (64 columns of f16) overwrote S of keys 0..63 only, which are
-          // still in registers; S of keys 64..127 is read again from TMEM so
-          // that its registers could be released early.
-          tmem_ld32(tS + 64u, sr[2]);
-          tmem_ld32(tS + 96u, sr[3]);
-          tmem_wait_ld();
-          prep(2);
-          prep(3);
-          tmem_wait_st();  // the speculative P stores land before they are overwritten
-          lsum = p_pass(kOffset - m, kNoTrack{}, smax);
-        }
       }
+      l *= alpha;
+      m = m_new;
+
+      // P = 2^(s*c - m + offset), two f32 MUFU ex2 per pair, stored over the
+      // first S columns as f16 pairs (PV16: 8 columns per 16 keys) or e4m3
+      // quads (4 columns); the row sum takes the unrounded f32 values.
+      const float nb = kOffset - m;
+      const float2 nn = make_float2(nb, nb);
+      float2 lsum2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int g16 = 0; g16 < 8; ++g16) {  // 16 keys per group
+        const int c = g16 >> 1, i0 = (g16 & 1) * 8;
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float2 x = ffma2(make_float2(u2f(sr[c][2 * (i0 + i)]), u2f(sr[c][2 * (i0 + i) + 1])), cc, nn);
+          const float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+          lsum2 = __fadd2_rn(lsum2, pp);
+          if constexpr (PV16) {
+            pk[i] = cvt_f16x2(pp.y, pp.x);
+          } else {
+            const uint32_t p2 = cvt_e4m3x2_f32(pp.y, pp.x);
+            if (i & 1)
+              pk[i >> 1] |= p2 << 16;
+            else
+              pk[i >> 1] = p2;
+          }
+        }
+        if constexpr (PV16)
+          tmem_st8(tS + (uint32_t)(g16 * 8), pk);
+        else
+          tmem_st4(tS + (uint32_t)(g16 * 4), pk);
+      }
+      const float lsum = lsum2.x + lsum2.y;
       l += lsum;
       tmem_wait_st();
       tc_fence_before();

@@ -347,38 +347,11 @@ __device__ __forceinline__ uint32_t cvt_f16x2(float hi, float lo) {
   return d;
 }
 
-__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
-  uint32_t y;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
-}
-
-__device__ __forceinline__ uint32_t hadd2(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
-// Two e4m3 values (low byte from the low half) from an f16x2, RNE, saturating.
-__device__ __forceinline__ uint32_t cvt_e4m3x2_f16x2(uint32_t x) {
-  uint16_t d;
-  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(d) : "r"(x));
-  return (uint32_t)d;
-}
-
 // Two e4m3 values from two floats: ``hi`` to the high byte, ``lo`` to the low.
 __device__ __forceinline__ uint32_t cvt_e4m3x2_f32(float hi, float lo) {
   uint16_t d;
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(d) : "f"(hi), "f"(lo));
   return (uint32_t)d;
-}
-
-__device__ __forceinline__ float2 f16x2_to_float2(uint32_t x) {
-  float lo, hi;
-  asm("{\n\t.reg .f16 l, h;\n\tmov.b32 {l, h}, %2;\n\tcvt.f32.f16 %0, l;\n\tcvt.f32.f16 %1, h;\n\t}"
-      : "=f"(lo), "=f"(hi)
-      : "r"(x));
-  return make_float2(lo, hi);
 }
 
 // Packed fp32 pair FMA: {a.x*b.x+c.x, a.y*b.y+c.y}.
@@ -391,44 +364,6 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
   float2 d;
   asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(ud));
   return d;
-}
-
-// Cubic minimax fit of 2^f on [0, 1] (Remez; max relative error 7.5e-5,
-// i.e. finer than the f16 rounding of P that follows).
-constexpr float kExp2C0 = 0.9999251961708069f;
-constexpr float kExp2C1 = 0.6958336234092712f;
-constexpr float kExp2C2 = 0.22606725990772247f;
-constexpr float kExp2C3 = 0.07802427560091019f;
-constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
-
-// 2^(s*c + nb) * w for a pair on the FMA pipe instead of MUFU.  The caller
-// folds the weight w into the Horner coefficients (k[i] = kExp2C<i> * w,
-// w in [1, 2), e.g. 2^frac(nb') for a non-integral offset nb').  Requirements:
-// nb is an integer with |nb| < 2^21, nbm = nb + kRoundMagic, and
-// s*c + nb >= -126 (so the exponent field below stays >= 0).
-//   t = RD(s*c + nbm)   -> low mantissa bits of t hold n = floor(s*c + nb)
-//   d = nbm - t = nb - n (exact: both are integers in [2^23, 2^24))
-//   f = s*c + d in [0, 1],  w*2^f by Horner,  2^n by adding n to the exponent.
-struct Exp2Coef {
-  float2 k0, k1, k2, k3;
-};
-
-__device__ __forceinline__ Exp2Coef exp2_coef(float w) {
-  return {make_float2(kExp2C0 * w, kExp2C0 * w), make_float2(kExp2C1 * w, kExp2C1 * w),
-          make_float2(kExp2C2 * w, kExp2C2 * w), make_float2(kExp2C3 * w, kExp2C3 * w)};
-}
-
-__device__ __forceinline__ float2 exp2_fma_pipe(float2 s, float2 c, float2 nbm, const Exp2Coef& k) {
-  const float2 t = __ffma2_rd(s, c, nbm);
-  const float2 d = __ffma2_rn(t, make_float2(-1.0f, -1.0f), nbm);
-  const float2 f = __ffma2_rn(s, c, d);
-  float2 q = __ffma2_rn(k.k3, f, k.k2);
-  q = __ffma2_rn(q, f, k.k1);
-  q = __ffma2_rn(q, f, k.k0);
-  // (bits(t) << 23) == n << 23 (mod 2^32): the magic's own bits shift out.
-  const uint32_t ex = (__float_as_uint(t.x) << 23) + __float_as_uint(q.x);
-  const uint32_t ey = (__float_as_uint(t.y) << 23) + __float_as_uint(q.y);
-  return make_float2(__uint_as_float(ex), __uint_as_float(ey));
 }
 
 }  // namespace mh3
