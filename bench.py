@@ -516,6 +516,36 @@ def run_linear_workload(args):
                       "peak": peaks, "results": lines}), flush=True)
 
 
+def run_quant_workload(args):
+    """Drop-in Q/K/V quantisation at config 2 shapes (HBM-bound; not the headline).
+
+    ``mh3_quantize_qkv`` on bf16 q, k, v [1, 40, 32760, 128] (the reference's
+    per-128-row Q/K blocks, K centred on its channel mean, V per channel,
+    kernels/fp8_attention.py:39-170,338), V out as f16 (the default PV
+    operand) and as e4m3.  Algorithmic bytes: q, k, v read once (bf16) and
+    q8, k8, v8 written once; the kernels read K and V twice (statistics pass,
+    then the quantising pass), which ``bytes_moved`` counts.
+    """
+    from minimaxh3_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev)
+    q, k, v = _synthetic_qkv(dev)
+    n = q.numel()
+    peaks = _peaks()
+    lines = []
+    for vd, vbytes in ((torch.float16, 2), (torch.float8_e4m3fn, 1)):
+        ms = _time_cuda(lambda: ops.quantize_qkv(q, k, v, 1.4426950408889634 / math.sqrt(D), v_dtype=vd),
+                        args.steps, args.warmup, stream)
+        algo = n * (3 * 2 + 1 + 1 + vbytes)
+        moved = n * (5 * 2 + 1 + 1 + vbytes)
+        lines.append({"v_out": str(vd).replace("torch.", ""), "ms": ms, "algorithmic_bytes": algo,
+                      "achieved_gbs": algo / ms / 1e6, "frac_of_hbm": algo / ms / 1e6 / peaks["hbm_gbs"],
+                      "bytes_moved": moved, "moved_gbs": moved / ms / 1e6})
+    print(json.dumps({"workload": "config2 drop-in quantisation: bf16 q,k,v [1,40,32760,128] -> e4m3 + scales",
+                      "unit": "GB/s", "peak_hbm_gbs": peaks["hbm_gbs"], "results": lines}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -526,7 +556,7 @@ def main():
     ap.add_argument("--heads", type=int, default=40, help="heads (40 = config 2; fewer for ncu captures)")
     ap.add_argument("--no-extras", action="store_true",
                     help="kernel timing only (no e2e, no CPU baseline): the ncu capture command")
-    ap.add_argument("--workload", default="attention", choices=["attention", "linear"],
+    ap.add_argument("--workload", default="attention", choices=["attention", "linear", "quant"],
                     help="attention = config 2 (the headline line); linear = config 4 measurements")
     ap.add_argument("--pv", default="f16", choices=["f16", "e4m3"],
                     help="PV product operands: f16 P/V (default, meets the tolerance) or e4m3")
@@ -536,6 +566,9 @@ def main():
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         run_reference_arm(args, rank)
+        return
+    if args.workload == "quant":
+        run_quant_workload(args)
         return
     if args.workload == "linear":
         run_linear_workload(args)

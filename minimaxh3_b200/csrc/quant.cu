@@ -44,6 +44,24 @@ __device__ __forceinline__ void load8(const T* p, float (&x)[8]) {
   }
 }
 
+// 8 packed 16-bit values -> floats (same conversion as load8).
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (std::is_same<T, __half>::value) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      x[2 * i] = f.x;
+      x[2 * i + 1] = f.y;
+    } else {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+      x[2 * i] = f.x;
+      x[2 * i + 1] = f.y;
+    }
+  }
+}
+
 __device__ __forceinline__ float clamp448(float x) { return fminf(fmaxf(x, -448.0f), 448.0f); }
 
 // 8 floats -> 8 e4m3 bytes (element 0 in the lowest byte).
@@ -136,11 +154,15 @@ enum Mode { kQ = 0, kK = 1, kV = 2 };
 
 // One 128-row block of one (b, h): transform, block absmax (Q, K), divide,
 // clamp, e4m3.  Output contiguous [B,H,S,D]; scale [B,H,nblk].
+// The block is held as raw 16-byte row pieces (8 channels x R rows per
+// thread, 4 registers each) and converted twice - once for the absmax, once
+// for the output - so that three CTAs fit on an SM and keep enough loads in
+// flight for HBM.
 template <typename T, int D, int MODE, bool OUT_F16 = false>
-__global__ void __launch_bounds__(kThreads) block_quant_kernel(const T* __restrict__ x, long long sb, long long sh,
-                                                               long long ss, int S, int H, float premul,
-                                                               const float* __restrict__ chan /* mean or sv */,
-                                                               uint8_t* __restrict__ out, float* __restrict__ scale) {
+__global__ void __launch_bounds__(kThreads, 3) block_quant_kernel(const T* __restrict__ x, long long sb, long long sh,
+                                                                  long long ss, int S, int H, float premul,
+                                                                  const float* __restrict__ chan /* mean or sv */,
+                                                                  uint8_t* __restrict__ out, float* __restrict__ scale) {
   constexpr int CG = D / 8;
   constexpr int RL = kThreads / CG;
   constexpr int R = kBlockRows / RL;  // rows per thread
@@ -151,35 +173,45 @@ __global__ void __launch_bounds__(kThreads) block_quant_kernel(const T* __restri
   const int cg = threadIdx.x % CG, rl = threadIdx.x / CG;
   const T* xp = x + b * sb + h * sh + cg * 8;
   const long long bh = (long long)b * H + h;
-  float c8[8];
-  if (MODE != kQ) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) c8[i] = chan[bh * D + cg * 8 + i];
-  }
-  float v[R][8];
-  float amax = 0.0f;
+  uint4 raw[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const int row = blk * kBlockRows + rl + r * RL;
-    if (row < S) {
-      load8(xp + (long long)row * ss, v[r]);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (MODE == kQ) v[r][i] = v[r][i] * premul;   // fp8_attention.py:69
-        if (MODE == kK) v[r][i] = v[r][i] - c8[i];    // :111
-        amax = fmaxf(amax, fabsf(v[r][i]));
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[r][i] = 0.0f;     // masked rows are 0 (:69, :111)
-    }
+    raw[r] = row < S ? __ldg(reinterpret_cast<const uint4*>(xp + (long long)row * ss)) : make_uint4(0u, 0u, 0u, 0u);
   }
+  float c8[8];
+  if (MODE != kQ) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) c8[i] = __ldg(chan + bh * D + cg * 8 + i);
+  }
+  // transform (masked rows are 0, fp8_attention.py:69, :111)
+  auto value = [&](int r, float (&v)[8]) {
+    const int row = blk * kBlockRows + rl + r * RL;
+    unpack8<T>(raw[r], v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (MODE == kQ) v[i] = v[i] * premul;                 // :69
+      if (MODE == kK) v[i] = row < S ? v[i] - c8[i] : 0.0f;  // :111
+    }
+  };
   float s = 1.0f;
   if (MODE != kV) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float v[8];
+      value(r, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    }
     const float bm = block_max(amax, red);             // :70, :112
     s = fmaxf(bm, 1.0e-12f) / 448.0f;                  // :71, :113
     if (threadIdx.x == 0) scale[bh * nblk + blk] = s;
   }
+  // Convert again from the raw pieces instead of keeping R*8 floats alive
+  // across the reduction (the empty asm hides the first conversion from CSE).
+#pragma unroll
+  for (int r = 0; r < R; ++r) asm volatile("" : "+r"(raw[r].x), "+r"(raw[r].y), "+r"(raw[r].z), "+r"(raw[r].w));
   constexpr int ES = OUT_F16 ? 2 : 1;  // output element size
   uint8_t* op = out + ((bh * S) * D + cg * 8) * ES;
 #pragma unroll
@@ -187,8 +219,9 @@ __global__ void __launch_bounds__(kThreads) block_quant_kernel(const T* __restri
     const int row = blk * kBlockRows + rl + r * RL;
     if (row < S) {
       float y[8];
+      value(r, y);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) y[i] = clamp448(__fdiv_rn(v[r][i], MODE == kV ? c8[i] : s));  // :72, :114, :167
+      for (int i = 0; i < 8; ++i) y[i] = clamp448(__fdiv_rn(y[i], MODE == kV ? c8[i] : s));  // :72, :114, :167
       if constexpr (OUT_F16) {
         uint4 u;
         u.x = cvt_f16x2(y[1], y[0]);
