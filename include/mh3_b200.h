@@ -241,6 +241,29 @@ MH3_API int mh3_scaled_gemm(const mh3_gemm_args* args, void* stream);
  */
 MH3_API int mh3_widen_e4m3_to_f16(const void* src, void* dst, int64_t n, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Per-(batch, head) quantisation (BASELINE configs 2/3/5 scale granularity) */
+/* ------------------------------------------------------------------------ */
+/*
+ * The per-(batch, head) form of the reference's Q/K/V quantisation
+ * (kernels/fp8_attention.py:39-170 with one scale per (b,h) instead of per
+ * 128-row block), as a sequence-sharded DiT block holds it: x is [B, S, H, D]
+ * bf16/f16 under element strides sb/ss/sh (D contiguous, strides multiples
+ * of 8, 16-byte aligned).
+ *
+ * mh3_absmax_bh: amax[b*H+h] = max |x[b,:,h,:]| (f32 [B,H]; overwritten).
+ * mh3_quantize_bh: y = x / scale[b*H+h] (IEEE division) rounded to e4m3
+ * (after clamping to +-448) or f16 (out_dtype), written head-group-major:
+ * out [groups, B, S, H/groups, D] contiguous, head h in group h/(H/groups) -
+ * the send buffer of a head-parallel (Ulysses) all-to-all; groups = 1 gives
+ * plain [B, S, H, D].
+ */
+MH3_API int mh3_absmax_bh(const void* x, int32_t in_dtype, int64_t B, int64_t S, int64_t H, int64_t D, int64_t sb,
+                          int64_t ss, int64_t sh, float* amax, void* stream);
+MH3_API int mh3_quantize_bh(const void* x, int32_t in_dtype, int64_t B, int64_t S, int64_t H, int64_t D, int64_t sb,
+                            int64_t ss, int64_t sh, const float* scale, int32_t out_dtype, int32_t groups, void* out,
+                            void* stream);
+
 #ifdef __cplusplus
 }
 #endif

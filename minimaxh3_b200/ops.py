@@ -300,11 +300,59 @@ def widen_e4m3_to_f16(x8: torch.Tensor) -> torch.Tensor:
     x8 = x8.contiguous()
     out = torch.empty(x8.shape, dtype=torch.float16, device=x8.device)
     n = x8.numel()
-    if n % 16 or x8.data_ptr() % 16:
-        return x8.to(torch.float16)
+    if n % 16:
+        raise ValueError("widen_e4m3_to_f16 needs a multiple of 16 elements")
+    if x8.data_ptr() % 16:
+        x8 = x8.clone()  # fresh allocations are 16-byte aligned
     with torch.cuda.device(x8.device):
         rc = lib.mh3_widen_e4m3_to_f16(x8.data_ptr(), out.data_ptr(), n, _stream(x8.device))
     _lib.check(rc, "mh3_widen_e4m3_to_f16")
+    return out
+
+
+def _bh_args(x: torch.Tensor):
+    if not x.is_cuda or x.dim() != 4 or x.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("expected a CUDA bf16/f16 tensor [B, S, H, D]")
+    if x.stride(-1) != 1 or x.data_ptr() % 16 or any(st % 8 for st in x.stride()[:3]):
+        x = x.contiguous()
+    B, S, H, D = x.shape
+    return x, (x.data_ptr(), _dtype_code(x.dtype), B, S, H, D, x.stride(0), x.stride(1), x.stride(2))
+
+
+def absmax_bh(x: torch.Tensor) -> torch.Tensor:
+    """max |x[b, :, h, :]| as float32 [B, H] for x [B, S, H, D] (``mh3_absmax_bh``)."""
+    lib = _lib.load()
+    x, args = _bh_args(x)
+    out = torch.empty((x.shape[0], x.shape[2]), dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        rc = lib.mh3_absmax_bh(*args, out.data_ptr(), _stream(x.device))
+    _lib.check(rc, "mh3_absmax_bh")
+    return out
+
+
+def quantize_bh(x: torch.Tensor, scale: torch.Tensor, out_dtype: torch.dtype = E4M3, groups: int = 1,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """x [B,S,H,D] / scale[b,h] -> e4m3 (clamped to +-448) or f16, as
+    [groups, B, S, H/groups, D] (head h in group h // (H/groups)); ``mh3_quantize_bh``."""
+    lib = _lib.load()
+    x, args = _bh_args(x)
+    B, S, H, D = x.shape
+    if out_dtype not in (E4M3, torch.float16):
+        raise ValueError("out_dtype must be float8_e4m3fn or float16")
+    if groups <= 0 or H % groups:
+        raise ValueError("groups must divide the head count")
+    scale = scale.to(device=x.device, dtype=torch.float32).contiguous()
+    if scale.numel() != B * H:
+        raise ValueError("scale must hold B*H values")
+    shape = (groups, B, S, H // groups, D)
+    if out is None:
+        out = torch.empty(shape, dtype=out_dtype, device=x.device)
+    elif tuple(out.shape) != shape or out.dtype != out_dtype or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous {out_dtype} tensor of shape {shape}")
+    code = _lib.MH3_DTYPE_F16 if out_dtype == torch.float16 else _lib.MH3_DTYPE_E4M3
+    with torch.cuda.device(x.device):
+        rc = lib.mh3_quantize_bh(*args, scale.data_ptr(), code, int(groups), out.data_ptr(), _stream(x.device))
+    _lib.check(rc, "mh3_quantize_bh")
     return out
 
 

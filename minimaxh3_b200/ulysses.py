@@ -6,16 +6,18 @@ parallelism; BASELINE config 5 asks for S=75600 self-attention sharded over
 ``[B, S_local, H, D]`` (the layout a sequence-parallel DiT block holds).  Per
 call:
 
-1. per-(batch, head) absmax of the local shard, one ``all_reduce(MAX)`` of
-   3*B*H floats, so every rank quantises with the global per-(b,h) scale
-   (BASELINE configs 2/3/5 use per-(b,h) scales);
+1. per-(batch, head) absmax of the local shard (``mh3_absmax_bh``), one
+   ``all_reduce(MAX)`` of 3*B*H floats, so every rank quantises with the
+   global per-(b,h) scale (BASELINE configs 2/3/5 use per-(b,h) scales);
 2. local e4m3 quantisation (V: f16 V/scale for the f16 PV product, or e4m3)
-   straight into the send layout ``[P, B, S_local, H/P, D]``;
+   straight into the send layout ``[P, B, S_local, H/P, D]``
+   (``mh3_quantize_bh``, one read of the bf16 shard, no fp32 temporaries);
 3. one NCCL ``all_to_all_single`` per tensor: rank r receives every rank's
    tokens for heads ``[r*H/P, (r+1)*H/P)``; for B = 1 the receive buffer is
    already ``[S, H/P, D]`` in global token order and the attention kernel
    reads it in place through its strided TMA maps;
-4. local FP8 attention over H/P heads, written as ``[P, S_local, H/P, D]``;
+4. local FP8 attention over H/P heads, written (B = 1: by the kernel itself,
+   through output strides) into the send buffer ``[P, B, S_local, H/P, D]``;
 5. one bf16 ``all_to_all_single`` back and a head interleave to
    ``[B, S_local, H, D]``.
 
@@ -23,8 +25,9 @@ Only steps 1, 3 and 5 communicate; the e4m3 all-to-all moves half the bytes
 of a bf16 one.  Cross-attention to replicated text K/V needs no collective:
 call ``fp8_attention`` on the local query shard.
 
-``attn_fn`` is injectable so the collective plumbing can be tested on CPU
-``gloo`` ranks with the oracle standing in for the kernel.
+``attn_fn``, ``absmax_fn`` and ``quant_fn`` are injectable so the collective
+plumbing can be tested on CPU ``gloo`` ranks with the oracle standing in for
+the kernels; the defaults are the CUDA kernels and fail loudly without them.
 """
 from __future__ import annotations
 
@@ -41,26 +44,30 @@ def _world(group):
     return dist.get_world_size(group), dist.get_rank(group)
 
 
-def global_absmax(xs, group=None):
+def global_absmax(xs, group=None, absmax_fn=None):
     """[len(xs), B, H] float32 absmax over (S, D) of each [B,S_local,H,D], max-reduced over ranks."""
-    local = torch.stack([x.float().abs().amax(dim=(1, 3)) for x in xs])
+    fn = absmax_fn or _cuda_absmax
+    local = torch.stack([fn(x) for x in xs])
     dist.all_reduce(local, op=dist.ReduceOp.MAX, group=group)
     return local
 
 
-def _quant_to_send(x, scale, P, out_dtype):
-    """x [B,S_l,H,D] / scale[B,H] -> [P, B, S_l, H/P, D] (e4m3 clamp or f16)."""
-    B, S_l, H, D = x.shape
-    y = x.float() / scale[:, None, :, None]
-    if out_dtype == E4M3:
-        y = torch.clamp(y, -448.0, 448.0)
-    y = y.to(out_dtype)
-    return y.reshape(B, S_l, P, H // P, D).permute(2, 0, 1, 3, 4).contiguous()
+def _cuda_absmax(x):
+    from . import ops
+
+    return ops.absmax_bh(x)
 
 
-def _exchange(send, group):
+def _cuda_quant(x, scale, P, out_dtype):
+    """x [B,S_l,H,D] / scale[B,H] -> [P, B, S_l, H/P, D] (e4m3 clamp or f16): ``mh3_quantize_bh``."""
+    from . import ops
+
+    return ops.quantize_bh(x, scale, out_dtype=out_dtype, groups=P)
+
+
+def _exchange(send, group, recv=None):
     """all_to_all_single on the leading (rank) dimension; dtype-agnostic."""
-    recv = torch.empty_like(send)
+    recv = torch.empty_like(send) if recv is None else recv
     s8 = send.view(torch.uint8) if send.dtype == E4M3 else send
     r8 = recv.view(torch.uint8) if recv.dtype == E4M3 else recv
     dist.all_to_all_single(r8, s8, group=group)
@@ -75,31 +82,34 @@ def _head_major(recv):
     return recv.permute(1, 3, 0, 2, 4).reshape(B, Hl, P * S_l, D)
 
 
-def _default_attn(q8, k8, v, sq, sk, sv, logit_scale_log2):
+def _default_attn(q8, k8, v, sq, sk, sv, logit_scale_log2, out=None):
     from . import ops
 
-    return ops.attention_e4m3(q8, k8, v, sq, sk, sv, logit_scale_log2=logit_scale_log2)
+    return ops.attention_e4m3(q8, k8, v, sq, sk, sv, logit_scale_log2=logit_scale_log2, out=out)
 
 
-def ulysses_attention(q, k, v, group=None, scale=None, pv_dtype=torch.float16, attn_fn=None, events=None):
+def ulysses_attention(q, k, v, group=None, scale=None, pv_dtype=torch.float16, attn_fn=None, events=None,
+                      absmax_fn=None, quant_fn=None):
     """Head-parallel FP8 attention of sequence shards ``[B, S_local, H, D]``.
 
     Returns the local output shard ``[B, S_local, H, D]`` (bf16, like q's
     dtype).  H must be divisible by the world size; every rank must hold the
     same S_local.  ``events``: optional (start, end) CUDA events recorded
-    around the local attention kernel.
+    around the local attention kernel.  ``attn_fn`` / ``absmax_fn`` /
+    ``quant_fn`` replace the CUDA kernels (for CPU process groups in tests).
     """
     P, r = _world(group)
     B, S_l, H, D = q.shape
     if H % P:
         raise ValueError(f"heads ({H}) must be divisible by the world size ({P})")
     Hl = H // P
-    amax = global_absmax((q, k, v), group)                 # [3, B, H]
+    quant = quant_fn or _cuda_quant
+    amax = global_absmax((q, k, v), group, absmax_fn)       # [3, B, H]
     scales = torch.clamp(amax, min=1e-12) / 448.0
     sq_full, sk_full, sv_full = scales[0], scales[1], scales[2]
-    send_q = _quant_to_send(q, sq_full, P, E4M3)
-    send_k = _quant_to_send(k, sk_full, P, E4M3)
-    send_v = _quant_to_send(v, sv_full, P, pv_dtype)
+    send_q = quant(q, sq_full, P, E4M3)
+    send_k = quant(k, sk_full, P, E4M3)
+    send_v = quant(v, sv_full, P, pv_dtype)
     recv_q, recv_k, recv_v = (_exchange(t, group) for t in (send_q, send_k, send_v))
     hs = slice(r * Hl, (r + 1) * Hl)
     sq = sq_full[:, hs].contiguous()[..., None]            # [B, Hl, 1] per-(b,h)
@@ -108,12 +118,21 @@ def ulysses_attention(q, k, v, group=None, scale=None, pv_dtype=torch.float16, a
     ls2 = (scale if scale is not None else 1.0 / math.sqrt(D)) * LOG2E
     fn = attn_fn or _default_attn
     hq, hk, hv = _head_major(recv_q), _head_major(recv_k), _head_major(recv_v)
+    # The send buffer of the way back is [P, B, S_l, Hl, D]; for B = 1 the
+    # kernel writes it directly through strides (token s of head h at
+    # s*Hl*D + h*D).
+    send_o = torch.empty((P, B, S_l, Hl, D), dtype=q.dtype, device=q.device)
+    direct = B == 1 and attn_fn is None
     if events is not None:
         events[0].record()
-    o = fn(hq, hk, hv, sq, sk, sv, ls2)  # [B,Hl,S,D]
+    if direct:
+        fn(hq, hk, hv, sq, sk, sv, ls2, out=send_o.view(P * S_l, Hl, D).permute(1, 0, 2).unsqueeze(0))
+    else:
+        o = fn(hq, hk, hv, sq, sk, sv, ls2)  # [B,Hl,S,D]
     if events is not None:
         events[1].record()
-    # send back: chunk p = tokens of rank p -> [P, B, S_l, Hl, D]
-    send_o = o.to(q.dtype).permute(2, 0, 1, 3).reshape(P, S_l, B, Hl, D).permute(0, 2, 1, 3, 4).contiguous()
+    if not direct:
+        # chunk p = tokens of rank p -> [P, B, S_l, Hl, D]
+        send_o.copy_(o.to(q.dtype).permute(2, 0, 1, 3).reshape(P, S_l, B, Hl, D).permute(0, 2, 1, 3, 4))
     recv_o = _exchange(send_o, group)                       # [P(src heads), B, S_l, Hl, D]
     return recv_o.permute(1, 2, 0, 3, 4).reshape(B, S_l, H, D)

@@ -1,0 +1,43 @@
+"""Per-(batch, head) quantisation kernels (mh3_absmax_bh, mh3_quantize_bh) vs a torch restatement."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _restated(x, scale, P, out_dtype):
+    B, S, H, D = x.shape
+    y = x.float() / scale[:, None, :, None]
+    if out_dtype == torch.float8_e4m3fn:
+        y = torch.clamp(y, -448.0, 448.0)
+    return y.to(out_dtype).reshape(B, S, P, H // P, D).permute(2, 0, 1, 3, 4).contiguous()
+
+
+@pytest.mark.parametrize("B,S,H,D,P", [(1, 1000, 8, 128, 2), (2, 517, 6, 64, 3), (1, 37, 4, 128, 1)])
+@pytest.mark.parametrize("out_dtype", [torch.float8_e4m3fn, torch.float16])
+@pytest.mark.parametrize("in_dtype", [torch.bfloat16, torch.float16])
+def test_quantize_bh_bit_exact(B, S, H, D, P, out_dtype, in_dtype):
+    from minimaxh3_b200 import ops
+
+    g = torch.Generator(device="cuda").manual_seed(B * 1000 + S)
+    x = torch.randn(B, H, S, D, generator=g, device="cuda")
+    x[..., 3] *= 8.0
+    x = x.to(in_dtype).permute(0, 2, 1, 3)          # [B,S,H,D] view of [B,H,S,D] storage
+    amax = ops.absmax_bh(x)
+    assert torch.equal(amax, x.float().abs().amax(dim=(1, 3)))
+    scale = torch.clamp(amax, min=1e-12) / 448.0
+    got = ops.quantize_bh(x, scale, out_dtype=out_dtype, groups=P)
+    ref = _restated(x, scale, P, out_dtype)
+    assert got.shape == ref.shape
+    assert torch.equal(got.view(torch.uint8) if out_dtype != torch.float16 else got.view(torch.int16),
+                       ref.view(torch.uint8) if out_dtype != torch.float16 else ref.view(torch.int16))
+
+
+def test_bh_kernels_reject_bad_arguments():
+    from minimaxh3_b200 import ops
+
+    x = torch.zeros(1, 8, 6, 128, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        ops.quantize_bh(x, torch.ones(6, device="cuda"), groups=4)       # 4 does not divide 6
+    with pytest.raises(ValueError):
+        ops.absmax_bh(torch.zeros(1, 8, 6, 96, dtype=torch.bfloat16, device="cuda"))

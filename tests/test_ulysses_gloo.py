@@ -25,6 +25,20 @@ def _oracle_attn(q8, k8, v, sq, sk, sv, ls2):
     return OA.sdpa_dequant_oracle(qd, kd, vd, ls2, base2=True)
 
 
+def _oracle_absmax(x):
+    return x.float().abs().amax(dim=(1, 3))
+
+
+def _oracle_quant(x, scale, P, out_dtype):
+    """Restatement of mh3_quantize_bh: x [B,S_l,H,D] / scale[B,H] -> [P, B, S_l, H/P, D]."""
+    B, S_l, H, D = x.shape
+    y = x.float() / scale[:, None, :, None]
+    if out_dtype == torch.float8_e4m3fn:
+        y = torch.clamp(y, -448.0, 448.0)
+    y = y.to(out_dtype)
+    return y.reshape(B, S_l, P, H // P, D).permute(2, 0, 1, 3, 4).contiguous()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -46,7 +60,8 @@ def _worker(rank, world, port, B, S, H, D, pv, out_dir):
         q, k, v = _inputs(B, S, H, D)
         Sl = S // world
         sl = slice(rank * Sl, (rank + 1) * Sl)
-        out = ulysses_attention(q[:, sl], k[:, sl], v[:, sl], pv_dtype=pv, attn_fn=_oracle_attn)
+        out = ulysses_attention(q[:, sl], k[:, sl], v[:, sl], pv_dtype=pv, attn_fn=_oracle_attn,
+                                absmax_fn=_oracle_absmax, quant_fn=_oracle_quant)
         torch.save(out, os.path.join(out_dir, f"out{rank}.pt"))
     finally:
         dist.destroy_process_group()
@@ -107,6 +122,6 @@ def _bad_worker(rank, world, port, out_dir):
 
         x = torch.zeros(1, 8, 6, 64, dtype=torch.bfloat16)
         with pytest.raises(ValueError):
-            ulysses_attention(x, x, x, attn_fn=_oracle_attn)
+            ulysses_attention(x, x, x, attn_fn=_oracle_attn, absmax_fn=_oracle_absmax, quant_fn=_oracle_quant)
     finally:
         dist.destroy_process_group()
