@@ -61,7 +61,7 @@ def fp8_attention_host(
         dev = torch.device("cuda", torch.cuda.current_device())
     else:
         dev = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
-    hc = heads_per_chunk or max(1, min(H, -(-B * H // 20)))  # about 20 chunks (measured best)
+    hc = heads_per_chunk or max(1, min(H, -(-B * H // 40)))  # about 40 chunks (measured best)
     with torch.cuda.device(dev):
         _run(q, k, v, out, scale, key_mask, key_bias, hc, dev)
     return out
