@@ -178,6 +178,28 @@ def cpu_reference_sample(seconds: float = 10.0):
                       f"in {el:.1f}s (the reference's routed_sdpa CPU fallback)"}
 
 
+def cpu_config1():
+    """SURVEY config 1 on the host: routed_sdpa's torch SDPA fallback, fp32
+    q,k,v [1,8,1024,128] seed 0, 3 warm-ups then the median of 20."""
+    import platform
+    import statistics
+
+    from oracle.router_ref import cpu_sdpa_fallback
+
+    g = torch.Generator().manual_seed(0)
+    q, k, v = (torch.randn(1, 8, 1024, 128, generator=g) for _ in range(3))
+    for _ in range(3):
+        cpu_sdpa_fallback(q, k, v)
+    ts = []
+    for _ in range(20):
+        t0 = time.perf_counter()
+        cpu_sdpa_fallback(q, k, v)
+        ts.append(time.perf_counter() - t0)
+    med = statistics.median(ts)
+    return {"ms": med * 1e3, "tflops": 4.0 * 8 * 1024 * 1024 * 128 / med / 1e12, "cpu_count": os.cpu_count(),
+            "torch_threads": torch.get_num_threads(), "cpu": platform.processor() or platform.machine()}
+
+
 def run_reference_arm(args, rank):
     if rank != 0:
         return
@@ -412,6 +434,8 @@ def run_gpu_arm(args, dist, rank, world, local):
     if rank != 0:
         return
     cpu = cpu_reference_sample(seconds=args.cpu_seconds) if world == 1 else None
+    if cpu is not None:
+        cpu["config1"] = cpu_config1()
     line = {
         "metric": "FP8 attention TFLOPS (S=32760 H=40 D=128)",
         "value": value,
@@ -482,11 +506,12 @@ def run_linear_workload(args):
     dev = torch.device("cuda", 0)
     stream = torch.cuda.current_stream(dev)
     g = torch.Generator(device=dev).manual_seed(0)
-    M, K = 32760, 5120
-    x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+    M = 32760
+    xs = {}
     lines = []
     peaks = _peaks()
-    for N in (5120, 15360, 13824):
+    for N, K in ((5120, 5120), (15360, 5120), (13824, 5120), (5120, 13824)):  # last: MLP-down
+        x = xs.setdefault(K, torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16))
         lin = torch.nn.Linear(K, N, device=dev, dtype=torch.bfloat16)
         with torch.no_grad():
             lin.weight.copy_(torch.randn(N, K, generator=g, device=dev) * 0.02)
@@ -508,12 +533,104 @@ def run_linear_workload(args):
             return out + ((x @ A.t()) @ Bm.t()).to(out.dtype)
 
         t_ref = _time_cuda(ref_recipe, args.steps, args.warmup, stream)
-        lines.append({"N": N, "gemm_ms": t_gemm, "gemm_tflops": flop / t_gemm / 1e9,
+        t_cub = _time_cuda(lambda: torch._scaled_mm(x8, mod.w8.t(), scale_a=sa, scale_b=mod.w_scale, bias=mod.bias,
+                                                    out_dtype=torch.bfloat16), args.steps, args.warmup, stream)
+        lines.append({"N": N, "K": K, "gemm_ms": t_gemm, "gemm_tflops": flop / t_gemm / 1e9,
+                      "cublas_scaled_mm_tflops": flop / t_cub / 1e9,
                       "gemm_frac_of_fp8_peak": flop / t_gemm / 1e9 / peaks["fp8_tflops"],
                       "fp8linear_forward_ms": t_fwd, "fp8linear_forward_tflops": flop / t_fwd / 1e9,
                       "reference_recipe_ms": t_ref, "reference_recipe_tflops": flop / t_ref / 1e9})
-    print(json.dumps({"workload": "config4: FP8 scaled linear M=32760 K=5120, LoRA r=32", "unit": "TFLOP/s",
+    print(json.dumps({"workload": "config4: FP8 scaled linear M=32760 K=5120 (N 5120/15360/13824) and the MLP-down "
+                                  "shape K=13824 N=5120, LoRA r=32", "unit": "TFLOP/s",
                       "peak": peaks, "results": lines}), flush=True)
+
+
+def run_varlen_workload(args):
+    """packed varlen, cu_seqlens [0, 33784, 50676], H=40 D=128.
+
+    e4m3 q/k/v with per-(sequence, head) scales (synthetic N(0,1) with one
+    channel x8), f16 PV, bf16 out; attention is block-diagonal per sequence.
+    Algorithmic work 4*H*D*(33784^2 + 16892^2) = 2.922e13 FLOP per call.
+    """
+    from minimaxh3_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev)
+    lens = [33784, 16892]
+    T, Hh, Dd = sum(lens), 40, 128
+    g = torch.Generator(device=dev).manual_seed(0)
+    gc = torch.Generator().manual_seed(0)
+    cu = torch.tensor([0, lens[0], T], dtype=torch.int32, device=dev)
+    packed, scales = [], []
+    for _ in range(3):
+        x = torch.randn(T, Hh, Dd, generator=g, device=dev)
+        x[..., int(torch.randperm(Dd, generator=gc)[0])] *= 8.0
+        x = x.to(torch.bfloat16).float()
+        s = torch.stack([x[a:b].abs().amax(dim=(0, 2)) for a, b in ((0, lens[0]), (lens[0], T))])
+        s = torch.clamp(s, min=1e-12) / 448.0                       # [nseq, H]
+        seq_of = torch.repeat_interleave(torch.arange(2, device=dev), torch.tensor(lens, device=dev))
+        packed.append(torch.clamp(x / s[seq_of][..., None], -448, 448))
+        scales.append(s[..., None].contiguous())
+        del x
+    q8, k8 = (t.to(torch.float8_e4m3fn) for t in packed[:2])
+    v16 = packed[2].to(torch.float16)
+    del packed
+    ls2 = 1.4426950408889634 / math.sqrt(Dd)
+    out = torch.empty(T, Hh, Dd, dtype=torch.bfloat16, device=dev)
+    call = lambda: ops.attention_e4m3(q8, k8, v16, *scales, logit_scale_log2=ls2, cu_seqlens_q=cu,
+                                      cu_seqlens_k=cu, max_seqlen_q=max(lens), out=out)
+    ms = _time_cuda(call, args.steps, args.warmup, stream)
+    flop = 4.0 * Hh * Dd * sum(L * L for L in lens)
+    peaks = _peaks()
+    print(json.dumps({"workload": "config3: varlen cu_seqlens [0,33784,50676], H=40 D=128, per-(seq,head) "
+                                  "scales, f16 PV", "unit": "TFLOP/s", "ms": ms, "tflops": flop / ms / 1e9,
+                      "frac_of_fp8_peak": flop / ms / 1e9 / peaks["fp8_tflops"], "flop": flop}), flush=True)
+
+
+def run_block_workload(args):
+    """ms per synthetic DiT block at config 2 / 4 shapes (the full transformer
+    and its block count are not available): QKV projection FP8Linear
+    (5120 -> 15360), self-attention through the drop-in fp8_attention on
+    [1, 40, 32760, 128] views of it, out-projection FP8Linear (5120 -> 5120),
+    cross-attention of the 32760 tokens to 512 text tokens, MLP-up FP8Linear
+    (5120 -> 13824).  Random-init weights N(0, 0.02), bias N(0, 0.01), one
+    LoRA adapter r=32 on each linear, activations N(0, 1) bf16."""
+    from minimaxh3_b200.kernels.fp8_attention import fp8_attention
+    from minimaxh3_b200.kernels.fp8_linear import FP8Linear
+
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    M, C, Hh, Dd, T = 32760, 5120, 40, 128, 512
+
+    def lin(n_in, n_out):
+        layer = torch.nn.Linear(n_in, n_out, device=dev, dtype=torch.bfloat16)
+        with torch.no_grad():
+            layer.weight.copy_(torch.randn(n_out, n_in, generator=g, device=dev) * 0.02)
+            layer.bias.copy_(torch.randn(n_out, generator=g, device=dev) * 0.01)
+        mod = FP8Linear.from_linear(layer)
+        mod.adapters = [((torch.randn(32, n_in, generator=g, device=dev) * 0.01).to(torch.bfloat16),
+                         (torch.randn(n_out, 32, generator=g, device=dev) * 0.01).to(torch.bfloat16), 1.0)]
+        return mod
+
+    qkv, proj, mlp_up = lin(C, 3 * C), lin(C, C), lin(C, 13824)
+    x = torch.randn(M, C, generator=g, device=dev).to(torch.bfloat16)
+    tk, tv = (torch.randn(1, Hh, T, Dd, generator=g, device=dev).to(torch.bfloat16) for _ in range(2))
+
+    def block():
+        y = qkv(x).view(1, M, 3, Hh, Dd)
+        q, k, v = (y[:, :, i].transpose(1, 2) for i in range(3))   # [1, H, M, D] strided views
+        a = fp8_attention(q, k, v).transpose(1, 2).reshape(M, C)
+        h = proj(a)
+        c = fp8_attention(h.view(1, M, Hh, Dd).transpose(1, 2), tk, tv).transpose(1, 2).reshape(M, C)
+        return mlp_up(c)
+
+    ms = _time_cuda(block, args.steps, args.warmup, stream)
+    flop = (2.0 * M * C * (3 * C + C + 13824) + 4.0 * Hh * M * M * Dd + 4.0 * Hh * M * T * Dd)
+    print(json.dumps({"workload": "synthetic DiT block: QKV GEMM N=15360 + self-attention S=32760 + out-proj "
+                                  "N=5120 + cross-attention to 512 tokens + MLP-up N=13824 (LoRA r=32 on each "
+                                  "linear); per DiT step = this x num_blocks (num_blocks not available)",
+                      "unit": "ms", "ms_per_block": ms, "tflops": flop / ms / 1e9}), flush=True)
 
 
 def run_quant_workload(args):
@@ -556,7 +673,7 @@ def main():
     ap.add_argument("--heads", type=int, default=40, help="heads (40 = config 2; fewer for ncu captures)")
     ap.add_argument("--no-extras", action="store_true",
                     help="kernel timing only (no e2e, no CPU baseline): the ncu capture command")
-    ap.add_argument("--workload", default="attention", choices=["attention", "linear", "quant"],
+    ap.add_argument("--workload", default="attention", choices=["attention", "linear", "quant", "varlen", "block"],
                     help="attention = config 2 (the headline line); linear = config 4 measurements")
     ap.add_argument("--pv", default="f16", choices=["f16", "e4m3"],
                     help="PV product operands: f16 P/V (default, meets the tolerance) or e4m3")
@@ -569,6 +686,12 @@ def main():
         return
     if args.workload == "quant":
         run_quant_workload(args)
+        return
+    if args.workload == "varlen":
+        run_varlen_workload(args)
+        return
+    if args.workload == "block":
+        run_block_workload(args)
         return
     if args.workload == "linear":
         run_linear_workload(args)
