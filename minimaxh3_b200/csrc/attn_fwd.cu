@@ -17,11 +17,12 @@
 //    and V (default) or kind::f8f6f4 with e4m3 P and V.  V stays in its
 //    natural [key, channel] layout: the PV MMA reads it as an MN-major B
 //    operand, so no transposed copy of V is ever made.
-//  * MMA order per Q tile t and KV step j: as soon as the softmax has read
-//    S(t, j) into registers, S(t, j+1) for keys 64..127 (columns 64..127,
-//    which P never touches) is issued; after P(t, j): PV(t, j), then
-//    S(t, j+1) for keys 0..63.  The two Q tiles alternate, so the tensor core
-//    works on one tile while the other tile's softmax runs.
+//  * MMA order per Q tile t and KV step j: after P(t, j): PV(t, j), then
+//    S(t, j+1).  With e4m3 PV the upper half of S(t, j+1) (keys 64..127,
+//    columns P never touches) is issued earlier, as soon as the softmax has
+//    read S(t, j) into registers, and only the lower half follows PV.  The
+//    two Q tiles alternate, so the tensor core works on one tile while the
+//    other tile's softmax runs.
 //  * softmax (one thread per row): tile max, lazy running max (raised only
 //    when a tile's max exceeds it by a threshold, the idea of the reference's
 //    ``rowmax > m + 8`` at :267; the rare raise rescales the row of O in TMEM),
@@ -209,6 +210,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
       // ---------------------------------------------------------------- MMA issuer
       constexpr uint32_t kIdescS = idesc_e4m3(BM, BN, false, false);
       constexpr uint32_t kIdescS64 = idesc_e4m3(BM, BN / 2, false, false);
+      // Early upper half of the next S (see the header): pays with e4m3 PV;
+      // with f16 PV the tensor core is the busier side and two N=64 halves
+      // (Q read twice) cost more than one N=128 S after PV.
+#ifndef MH3_EARLY_HALF
+#define MH3_EARLY_HALF (PV16 ? 0 : 1)
+#endif
+      constexpr bool kEarlyHalf = MH3_EARLY_HALF;
       constexpr uint32_t kIdescO = PV16 ? idesc_f16(BM, D, false, true) : idesc_e4m3(BM, D, false, true);
       const uint32_t tS[2] = {tmem + 0u, tmem + 128u};
       const uint32_t tO[2] = {tmem + 256u, tmem + 256u + (uint32_t)D};
@@ -257,7 +265,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
         if (has_next) mbar_wait(smem_u32(&sm.bar_kfull[ks]), (uint32_t)((j + 1) / KST) & 1u, g);
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
-          if (has_next) {
+          if (kEarlyHalf && has_next) {
             mbar_wait(smem_u32(&sm.bar_sld[t]), (uint32_t)j & 1u, g);
             tc_fence_after();
             issue_s_half(t, ks, 1);
@@ -275,7 +283,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
           }
           if (t == 1) mma_commit(smem_u32(&sm.bar_vempty[vs]));
           if (has_next) {
-            issue_s_half(t, ks, 0);
+            if constexpr (kEarlyHalf)
+              issue_s_half(t, ks, 0);
+            else
+              issue_s(t, ks);
             mma_commit(smem_u32(&sm.bar_s[t]));
             if (t == 1) mma_commit(smem_u32(&sm.bar_kempty[ks]));
           }
