@@ -18,7 +18,8 @@
 //    natural [key, channel] layout: the PV MMA reads it as an MN-major B
 //    operand, so no transposed copy of V is ever made.
 //  * MMA order per Q tile t and KV step j: after P(t, j): PV(t, j), then
-//    S(t, j+1).  With e4m3 PV the upper half of S(t, j+1) (keys 64..127,
+//    S(t, j+1).  With f16 PV, P(t, j) is released in two key halves and the
+//    first half's PV runs while the softmax computes the second half.  With e4m3 PV the upper half of S(t, j+1) (keys 64..127,
 //    columns P never touches) is issued earlier, as soon as the softmax has
 //    read S(t, j) into registers, and only the lower half follows PV.  The
 //    two Q tiles alternate, so the tensor core works on one tile while the
@@ -55,6 +56,18 @@ constexpr float P_OFFSET8 = 4.0f;
 constexpr float LAZY_T16 = 12.0f;
 constexpr float P_OFFSET16 = 0.0f;
 
+// P(j) is handed to the PV MMAs in N key parts, each as soon as the softmax
+// has stored it.  With f16 PV (the tensor core the busier side) splitting
+// takes most of PV off the softmax -> PV -> S chain; with e4m3 PV the extra
+// store waits cost more than they save.
+#ifndef MH3_P_PARTS
+#define MH3_P_PARTS 2
+#endif
+template <bool PV16>
+struct PParts {
+  static constexpr int N = PV16 ? MH3_P_PARTS : 1;
+};
+
 struct Params {
   CUtensorMap tmq;  // e4m3 (D, S, H, B), box (D, 128, 1, 1)
   CUtensorMap tmk;
@@ -89,7 +102,7 @@ struct __align__(1024) Smem {
   uint64_t bar_vempty[VST];
   uint64_t bar_s[2];
   uint64_t bar_sld[2];  // softmax has read S(j) into registers
-  uint64_t bar_p[2];
+  uint64_t bar_p[2][4];  // [tile][key part]: that part of P(j) is in TMEM
   uint64_t bar_o;
   uint32_t tmem_base;
   int abort_flag;
@@ -146,7 +159,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&sm.bar_s[i]), 1);
       mbar_init(smem_u32(&sm.bar_sld[i]), 4);
-      mbar_init(smem_u32(&sm.bar_p[i]), 4);
+      for (int k = 0; k < 4; ++k) mbar_init(smem_u32(&sm.bar_p[i][k]), 4);
     }
     mbar_init(smem_u32(&sm.bar_o), 1);
     sm.abort_flag = 0;
@@ -217,6 +230,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
 #define MH3_EARLY_HALF (PV16 ? 0 : 1)
 #endif
       constexpr bool kEarlyHalf = MH3_EARLY_HALF;
+      constexpr int kPHalves = PParts<PV16>::N;
       constexpr uint32_t kIdescO = PV16 ? idesc_f16(BM, D, false, true) : idesc_e4m3(BM, D, false, true);
       const uint32_t tS[2] = {tmem + 0u, tmem + 128u};
       const uint32_t tO[2] = {tmem + 256u, tmem + 256u + (uint32_t)D};
@@ -270,16 +284,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
             tc_fence_after();
             issue_s_half(t, ks, 1);
           }
-          mbar_wait(smem_u32(&sm.bar_p[t]), (uint32_t)j & 1u, g);
-          tc_fence_after();
-          if constexpr (PV16) {
+          // PV in key parts, each issued as soon as the softmax has stored
+          // that part of P (only the last part follows the softmax).
 #pragma unroll
-            for (int kk = 0; kk < BN / 16; ++kk)
-              mma_f16_ts(tO[t], tS[t] + (uint32_t)(kk * 8), vdesc(vs, kk), kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
-          } else {
+          for (int hf = 0; hf < kPHalves; ++hf) {
+            mbar_wait(smem_u32(&sm.bar_p[t][hf]), (uint32_t)j & 1u, g);
+            tc_fence_after();
+            constexpr int kPer = (PV16 ? BN / 16 : BN / 32) / kPHalves;
+            if constexpr (PV16) {
 #pragma unroll
-            for (int kk = 0; kk < BN / 32; ++kk)
-              mma_f8_ts(tO[t], tS[t] + (uint32_t)(kk * 8), vdesc(vs, kk), kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+              for (int kk = hf * kPer; kk < hf * kPer + kPer; ++kk)
+                mma_f16_ts(tO[t], tS[t] + (uint32_t)(kk * 8), vdesc(vs, kk), kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+            } else {
+#pragma unroll
+              for (int kk = hf * kPer; kk < hf * kPer + kPer; ++kk)
+                mma_f8_ts(tO[t], tS[t] + (uint32_t)(kk * 8), vdesc(vs, kk), kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+            }
           }
           if (t == 1) mma_commit(smem_u32(&sm.bar_vempty[vs]));
           if (has_next) {
@@ -416,13 +436,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
           tmem_st8(tS + (uint32_t)(g16 * 8), pk);
         else
           tmem_st4(tS + (uint32_t)(g16 * 4), pk);
+        constexpr int kGroupsPerPart = 8 / PParts<PV16>::N;
+        if (g16 % kGroupsPerPart == kGroupsPerPart - 1) {  // a part of P is in TMEM: release it
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&sm.bar_p[t][g16 / kGroupsPerPart]));
+        }
       }
-      const float lsum = lsum2.x + lsum2.y;
-      l += lsum;
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&sm.bar_p[t]));
+      l += lsum2.x + lsum2.y;
     }
 
     // ---------------------------------------------------------------- epilogue
