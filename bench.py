@@ -51,9 +51,9 @@ NOMINAL_FP8_TFLOPS = 4500.0
 
 # DRAM bytes (read + write) of one config-2 attention launch from the ncu
 # capture summarised in profiles/attn_fwd_config2.md: H=8 measured
-# (134.5 MB read + 41.3 MB write), scaled to H=40 by the heads processed
+# (134.7 MB read + 43.6 MB write), scaled to H=40 by the heads processed
 # (each (batch, head) is an independent set of CTAs reading its own Q, K, V).
-ATTN_TRAFFIC_BYTES_H40 = {"f16": 5 * (134.476e6 + 41.250e6)}
+ATTN_TRAFFIC_BYTES_H40 = {"f16": 5 * (134.672e6 + 43.554e6)}
 
 
 def _peaks():
