@@ -32,7 +32,7 @@ extern "C" {
 #define MH3_API __attribute__((visibility("default")))
 #endif
 
-#define MH3_ABI_VERSION 1
+#define MH3_ABI_VERSION 2 /* 2: mh3_attn_args.kv_len */
 
 #define MH3_OK 0
 #define MH3_ERR_INVALID (-1)     /* bad argument: shape, stride, alignment, null pointer */
@@ -115,6 +115,9 @@ typedef struct mh3_attn_args {
   int64_t key_bias2_stride_b;
   int* err;            /* device error word, or NULL for the library's own */
   uint64_t timeout_ns; /* bound on every pipeline wait; 0 = 4 s */
+  /* Optional int32 [batch] on the device: keys at or past kv_len[b] are
+   * masked (a padded batch); the kernel skips their tiles.  NULL = none. */
+  const int32_t* kv_len;
 } mh3_attn_args;
 
 MH3_API int mh3_fp8_attention_fwd(const mh3_attn_args* args, void* stream);

@@ -47,7 +47,7 @@ class AttnArgs(ctypes.Structure):
         ("cu_seqlens_q", c_ptr), ("cu_seqlens_k", c_ptr),
         ("total_q", c_i64), ("total_k", c_i64),
         ("key_bias2", c_ptr), ("key_bias2_stride_b", c_i64),
-        ("err", c_ptr), ("timeout_ns", c_u64),
+        ("err", c_ptr), ("timeout_ns", c_u64), ("kv_len", c_ptr),
     ]
 
 

@@ -88,6 +88,7 @@ struct Params {
   long long kbias_sb;
   int* err;
   unsigned long long timeout_ns;
+  const int* kv_len;  // per-batch key count (padding past it is skipped), or null
 };
 
 template <int D, bool PV16>
@@ -136,6 +137,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
     k_len = p.cuk[b + 1] - k_start;
     bcoord = 0;
   }
+  if (p.kv_len != nullptr) k_len = min(k_len, max(0, __ldg(p.kv_len + b)));  // tiles past it are all masked
   const int qt0 = blockIdx.x * 2;
   if (qt0 * BM >= q_len) return;  // uniform over the CTA, before any barrier
   const int nk = (k_len + BN - 1) / BN;
@@ -620,6 +622,7 @@ extern "C" int mh3_fp8_attention_fwd(const mh3_attn_args* a, void* stream) {
   p.kbias_sb = a->key_bias2_stride_b;
   p.err = a->err ? a->err : device_error_word();
   p.timeout_ns = a->timeout_ns ? a->timeout_ns : 4000000000ull;
+  p.kv_len = a->kv_len;
 
   const int max_q = varlen ? a->max_seqlen_q : a->seqlen_q;
   const int q_tiles = (max_q + attn::BM - 1) / attn::BM;

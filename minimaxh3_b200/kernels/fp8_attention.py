@@ -88,16 +88,18 @@ def _fp8_attention_impl(q, k, v, scale, key_mask, key_bias, repair_tau):
     Sk = k.shape[2]
     c = (scale if scale is not None else 1.0 / math.sqrt(D)) * LOG2E
     q8, k8, v8, sq, sk, sv, _ = _ops.quantize_qkv(q, k, v, c, v_dtype=_pv_dtype())
-    bias2 = None
+    bias2 = kv_len = None
     if key_mask is not None or key_bias is not None:
         bias2 = _ops.build_key_bias2(key_mask, key_bias, B, Sk, q.device)
+        # padded batches: the tiles past each batch's last valid key are skipped
+        kv_len = _ops.key_valid_len(key_mask, key_bias, B, Sk, q.device)
     # Same strides as the reference's ``torch.empty_like(q)`` (:379); the
     # kernel writes through the strides, so transposed views stay correct.
     out = torch.empty_like(q)
     if out.stride(-1) != 1 or any(s % 8 for s in out.stride()[:3]):
         out = torch.empty((B, H, Sq, D), dtype=q.dtype, device=q.device)
     return _ops.attention_e4m3(q8, k8, v8, sq, sk, sv, logit_scale_log2=1.0, out_dtype=q.dtype,
-                               key_bias2=bias2, out=out)
+                               key_bias2=bias2, out=out, kv_len=kv_len)
 
 
 @torch.library.custom_op("mh3::fp8_attention", mutates_args=())

@@ -106,6 +106,7 @@ def attention_e4m3(
     out: torch.Tensor | None = None,
     err: torch.Tensor | None = None,
     timeout_ns: int = 0,
+    kv_len: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Non-causal FP8 attention (``mh3_fp8_attention_fwd``).
 
@@ -194,10 +195,29 @@ def attention_e4m3(
     if err is not None:
         a.err = err.data_ptr()
     a.timeout_ns = int(timeout_ns)
+    if kv_len is not None:
+        if kv_len.dtype != torch.int32 or kv_len.numel() < a.batch or not kv_len.is_cuda:
+            raise ValueError("kv_len must be a CUDA int32 tensor with one entry per batch")
+        kv_len = kv_len.contiguous()
+        a.kv_len = kv_len.data_ptr()
     with torch.cuda.device(q8.device):
         rc = lib.mh3_fp8_attention_fwd(a, _stream(q8.device))
     _lib.check(rc, "mh3_fp8_attention_fwd")
     return out
+
+
+def key_valid_len(key_mask, key_bias, B: int, Sk: int, device) -> torch.Tensor:
+    """int32 [B]: one past the last key that the mask / bias leaves valid
+    (0 when none is), computed on the device without a host sync.  Keys at
+    or past it are masked, so the kernel may skip their tiles (``kv_len``);
+    a padded batch then costs only its real keys."""
+    valid = torch.ones((B, Sk), dtype=torch.bool, device=device)
+    if key_bias is not None:
+        valid = valid & (key_bias.to(device=device, dtype=torch.float32).expand(B, Sk) > -1.0e8)
+    if key_mask is not None:
+        valid = valid & key_mask.to(device=device, dtype=torch.bool).expand(B, Sk)
+    idx = torch.arange(1, Sk + 1, dtype=torch.int32, device=device)
+    return torch.where(valid, idx, torch.zeros_like(idx)).amax(dim=1).to(torch.int32)
 
 
 def build_key_bias2(key_mask, key_bias, B: int, Sk: int, device) -> torch.Tensor:

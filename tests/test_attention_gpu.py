@@ -258,3 +258,32 @@ def test_widen_e4m3_to_f16_exact():
     nan = torch.isnan(ref)
     assert torch.equal(torch.isnan(got), nan)
     assert torch.equal(got[~nan], ref[~nan])
+
+
+@pytest.mark.parametrize("pv", ["f16", "e4m3"])
+def test_padded_batch_kv_len_skips_tiles_exactly(pv):
+    """A padded batch (valid keys = a prefix) through fp8_attention: the kernel
+    skips the tiles past each batch's last valid key (kv_len), bit-identical
+    to computing them masked, and matches the masked oracle."""
+    from minimaxh3_b200 import ops
+    from minimaxh3_b200.kernels.fp8_attention import fp8_attention
+
+    B, H, Sq, Sk, D = 3, 2, 300, 1000, 128
+    q, k, v = _inputs(13, B, H, Sq, Sk, D)
+    lens = torch.tensor([700, 1000, 131])
+    key_mask = torch.arange(Sk)[None, :] < lens[:, None]
+    out = fp8_attention(q.to(DEV), k.to(DEV), v.to(DEV), key_mask=key_mask.to(DEV)).float().cpu()
+    assert torch.isfinite(out).all()
+    kv = ops.key_valid_len(key_mask.to(DEV), None, B, Sk, DEV)
+    assert kv.cpu().tolist() == lens.tolist()
+    # same bytes through the kernel with and without the per-batch length
+    (q8, sq), (k8, sk), (v8, sv) = _per_bh(q), _per_bh(k), _per_bh(v)
+    ls2 = OA.LOG2E / math.sqrt(D)
+    bias2 = ops.build_key_bias2(key_mask.to(DEV), None, B, Sk, DEV)
+    args = (q8, k8, v8, sq[..., None], sk[..., None], sv[..., None], ls2)
+    full = _run_e4m3(*args, pv=pv, key_bias2=bias2)
+    skip = _run_e4m3(*args, pv=pv, key_bias2=bias2, kv_len=kv)
+    assert torch.equal(full, skip)
+    ref = OA.sdpa_dequant_oracle(q8.double() * sq[..., None, None], k8.double() * sk[..., None, None],
+                                 v8.double() * sv[..., None, None], ls2, key_mask=key_mask, base2=True)
+    _check(OA.compare(skip.float().cpu(), ref), pv)
