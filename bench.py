@@ -233,11 +233,13 @@ def run_reference_arm(args, rank):
 
 def run_ulysses_arm(args, dist, rank, world, local):
     from minimaxh3_b200.kernels.fp8_attention import fp8_attention
-    from minimaxh3_b200.ulysses import ulysses_attention
+    from minimaxh3_b200.ulysses import default_head_groups, ulysses_attention, ulysses_attention_host
 
     dev = torch.device("cuda", local)
     S5, H5, D5, T = 75600, 40, 128, 512
     Sl = S5 // world
+    G = args.head_groups
+    G_host = args.host_head_groups or default_head_groups(H5 // world)
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     gc = torch.Generator().manual_seed(0)
     shard = []
@@ -251,11 +253,11 @@ def run_ulysses_arm(args, dist, rank, world, local):
     flop_self = 4.0 * H5 * S5 * S5 * D5
     flop_cross = 4.0 * H5 * S5 * T * D5
     stream = torch.cuda.current_stream(dev)
-    attn_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(args.steps)]
+    attn_ev = []                                  # (start, end) around every local attention launch
+    o_buf = torch.empty_like(q)
 
     def step(ev=None):
-        o = ulysses_attention(q, k, v, events=ev)
+        o = ulysses_attention(q, k, v, events=ev, head_groups=G, out=o_buf)
         c = fp8_attention(q.transpose(1, 2), kt, vt)
         return o, c
 
@@ -269,7 +271,7 @@ def run_ulysses_arm(args, dist, rank, world, local):
     with ClockSampler(local) as clk:
         t0.record(stream)
         for i in range(args.steps):
-            step(attn_ev[i])
+            step(attn_ev)
         t1.record(stream)
         torch.cuda.synchronize(dev)
     dist.barrier()
@@ -281,20 +283,13 @@ def run_ulysses_arm(args, dist, rank, world, local):
     value = (flop_self + flop_cross) * args.steps / (ms / 1e3) / 1e12
     achieved = flop_self / world / (attn_ms / 1e3) / 1e12
     peaks = _peaks()
-    # e2e: the local shard comes from pinned host memory and the output goes back
+    # e2e: the local shard comes from pinned host memory and both outputs go
+    # back, each head group's copies overlapping the other groups' compute
     hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
-    ho = torch.empty_like(hq).pin_memory()
-    hc = torch.empty((1, H5, Sl, D5), dtype=torch.bfloat16).pin_memory()
-    dq, dk, dv = (torch.empty_like(x) for x in (q, k, v))
+    ho, hc = (torch.empty_like(hq).pin_memory() for _ in range(2))
 
     def e2e_step():
-        dq.copy_(hq, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dv.copy_(hv, non_blocking=True)
-        o = ulysses_attention(dq, dk, dv)
-        c = fp8_attention(dq.transpose(1, 2), kt, vt)
-        ho.copy_(o, non_blocking=True)
-        hc.copy_(c, non_blocking=True)
+        ulysses_attention_host(hq, hk, hv, out=ho, head_groups=G_host, cross_kv=(kt, vt), cross_out=hc)
 
     e2e_step()
     torch.cuda.synchronize(dev)
@@ -319,17 +314,19 @@ def run_ulysses_arm(args, dist, rank, world, local):
         "dtype": "e4m3 QK^T, f16 PV", "data": "synthetic",
         "config": {"workload": f"config5: Ulysses self-attention B=1 H=40 S=75600 D=128 over {world} GPUs "
                                f"(S/P={Sl}, H/P={H5 // world}) + cross-attention to 512 text tokens",
-                   "parallelism": f"ulysses{world}", "inputs_vs_l2": "per-rank inputs > 126 MB L2 (no flush)"},
+                   "parallelism": f"ulysses{world}", "head_groups": G, "e2e_head_groups": G_host,
+                   "inputs_vs_l2": "per-rank inputs > 126 MB L2 (no flush)"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["fp8_tflops"], "unit": "TFLOP/s",
                      "frac": achieved / peaks["fp8_tflops"], "traffic": None, "peak_source": peaks["source"],
-                     "kernel": "mh3::attn::fwd_kernel (local head shard)", "avg_launch_ms": attn_ms},
+                     "kernel": "mh3::attn::fwd_kernel (local head shard, one launch per head group)",
+                     "avg_launch_ms": attn_ms / G, "launches_per_step": G},
         "e2e": {"value": (flop_self + flop_cross) * n_e2e / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": 3 * Sl * H5 * D5 * 2 * world,
                 "d2h_bytes_per_step": 2 * Sl * H5 * D5 * 2 * world,
-                "api": "minimaxh3_b200.ulysses.ulysses_attention + kernels.fp8_attention.fp8_attention"},
-        # per step: local attention + the cross-attention's 5 quantisation
-        # kernels and 1 attention kernel
-        "gpu_launches": 7 * args.steps, "clocks": clk.summary(),
+                "api": "minimaxh3_b200.ulysses.ulysses_attention_host (cross_kv: fp8_attention per head group)"},
+        # per step and head group: 3 absmax + 3 quantize_bh + 1 attention;
+        # per step: the cross-attention's 5 quantisation kernels + 1 attention
+        "gpu_launches": (7 * G + 6) * args.steps, "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)
 
@@ -677,6 +674,10 @@ def main():
                     help="attention = config 2 (the headline line); linear = config 4 measurements")
     ap.add_argument("--pv", default="f16", choices=["f16", "e4m3"],
                     help="PV product operands: f16 P/V (default, meets the tolerance) or e4m3")
+    ap.add_argument("--head-groups", type=int, default=1,
+                    help="N>1: head groups of the device-resident Ulysses pipeline (the value line)")
+    ap.add_argument("--host-head-groups", type=int, default=0,
+                    help="N>1: head groups of the host-resident e2e pipeline (0 = ulysses.default_head_groups)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "mh3":
         args.warmup = 3

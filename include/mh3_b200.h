@@ -32,7 +32,7 @@ extern "C" {
 #define MH3_API __attribute__((visibility("default")))
 #endif
 
-#define MH3_ABI_VERSION 2 /* 2: mh3_attn_args.kv_len */
+#define MH3_ABI_VERSION 3 /* 2: mh3_attn_args.kv_len; 3: head selection in mh3_absmax_bh / mh3_quantize_bh, mh3_copy_rows */
 
 #define MH3_OK 0
 #define MH3_ERR_INVALID (-1)     /* bad argument: shape, stride, alignment, null pointer */
@@ -254,18 +254,37 @@ MH3_API int mh3_widen_e4m3_to_f16(const void* src, void* dst, int64_t n, void* s
  * bf16/f16 under element strides sb/ss/sh (D contiguous, strides multiples
  * of 8, 16-byte aligned).
  *
- * mh3_absmax_bh: amax[b*H+h] = max |x[b,:,h,:]| (f32 [B,H]; overwritten).
- * mh3_quantize_bh: y = x / scale[b*H+h] (IEEE division) rounded to e4m3
- * (after clamping to +-448) or f16 (out_dtype), written head-group-major:
- * out [groups, B, S, H/groups, D] contiguous, head h in group h/(H/groups) -
- * the send buffer of a head-parallel (Ulysses) all-to-all; groups = 1 gives
- * plain [B, S, H, D].
+ * Head selection: the H heads form P = H/head_block blocks (one per rank of
+ * a head-parallel group); selected are heads p*head_block + head_off + i for
+ * every block p and i < heads_sel, numbered j = p*heads_sel + i (nsel =
+ * P*heads_sel).  All heads: head_block = heads_sel = H, head_off = 0.
+ *
+ * mh3_absmax_bh: amax[b*nsel+j] = max |x[b,:,head(j),:]| (f32; overwritten).
+ * mh3_quantize_bh: y = x / scale[b*nsel+j] (IEEE division) rounded to e4m3
+ * (after clamping to +-448) or f16 (out_dtype), written block-major: out
+ * [P, B, S, heads_sel, D] contiguous - the send buffer of a head-parallel
+ * (Ulysses) all-to-all, for all of a rank's heads or for a group of them.
  */
 MH3_API int mh3_absmax_bh(const void* x, int32_t in_dtype, int64_t B, int64_t S, int64_t H, int64_t D, int64_t sb,
-                          int64_t ss, int64_t sh, float* amax, void* stream);
+                          int64_t ss, int64_t sh, int32_t head_block, int32_t head_off, int32_t heads_sel,
+                          float* amax, void* stream);
 MH3_API int mh3_quantize_bh(const void* x, int32_t in_dtype, int64_t B, int64_t S, int64_t H, int64_t D, int64_t sb,
-                            int64_t ss, int64_t sh, const float* scale, int32_t out_dtype, int32_t groups, void* out,
-                            void* stream);
+                            int64_t ss, int64_t sh, int32_t head_block, int32_t head_off, int32_t heads_sel,
+                            const float* scale, int32_t out_dtype, void* out, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Strided host<->device row copies                                         */
+/* ------------------------------------------------------------------------ */
+/*
+ * rows x row_bytes from src (row pitch src_pitch bytes) to dst (row pitch
+ * dst_pitch bytes), asynchronously on ``stream``, either direction between
+ * pinned host memory and device memory (or device to device).  Moves one
+ * head group of a host-resident [B, S, H, D] shard - a run of heads in every
+ * token row - without staging it through a contiguous host copy.  No
+ * reference counterpart (the reference's tensors are device-resident).
+ */
+MH3_API int mh3_copy_rows(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch, int64_t row_bytes,
+                          int64_t rows, void* stream);
 
 #ifdef __cplusplus
 }

@@ -92,9 +92,11 @@ _SIGNATURES = {
     "mh3_quantize_rows": (c_i32, [c_ptr, c_i64, c_i32, c_i64, c_i64, c_ptr, c_ptr, c_ptr]),
     "mh3_widen_e4m3_to_f16": (c_i32, [c_ptr, c_ptr, c_i64, c_ptr]),
     "mh3_scaled_gemm": (c_i32, [ctypes.POINTER(GemmArgs), c_ptr]),
-    "mh3_absmax_bh": (c_i32, [c_ptr, c_i32, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_ptr, c_ptr]),
-    "mh3_quantize_bh": (c_i32, [c_ptr, c_i32, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_ptr, c_i32, c_i32,
-                                c_ptr, c_ptr]),
+    "mh3_absmax_bh": (c_i32, [c_ptr, c_i32, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i32, c_i32, c_i32,
+                              c_ptr, c_ptr]),
+    "mh3_quantize_bh": (c_i32, [c_ptr, c_i32, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i32, c_i32, c_i32,
+                                c_ptr, c_i32, c_ptr, c_ptr]),
+    "mh3_copy_rows": (c_i32, [c_ptr, c_i64, c_ptr, c_i64, c_i64, c_i64, c_ptr]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

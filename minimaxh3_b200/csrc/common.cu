@@ -74,3 +74,13 @@ extern "C" int mh3_abi_version(void) { return MH3_ABI_VERSION; }
 extern "C" const char* mh3_last_error(void) { return mh3::g_last_error.c_str(); }
 
 extern "C" int* mh3_device_error_word(void) { return mh3::device_error_word(); }
+
+extern "C" int mh3_copy_rows(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch, int64_t row_bytes,
+                             int64_t rows, void* stream) {
+  if (rows == 0 || row_bytes == 0) return MH3_OK;
+  if (dst == nullptr || src == nullptr || rows < 0 || row_bytes < 0 || dst_pitch < row_bytes || src_pitch < row_bytes)
+    return mh3::fail(MH3_ERR_INVALID, "mh3_copy_rows: bad pointers, pitches or sizes");
+  cudaError_t e = cudaMemcpy2DAsync(dst, (size_t)dst_pitch, src, (size_t)src_pitch, (size_t)row_bytes, (size_t)rows,
+                                    cudaMemcpyDefault, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MH3_OK : mh3::fail_cuda(e, "mh3_copy_rows");
+}

@@ -312,17 +312,26 @@ __global__ void widen_e4m3_f16_kernel(const uint4* __restrict__ src, uint4* __re
   }
 }
 
+// Head selection shared by the two per-(batch, head) kernels: the H heads
+// form H/hb blocks of hb; selected are heads p*hb + off + i for every block p
+// and i < hs, numbered j = p*hs + i (hb = hs = H, off = 0: all heads).
+struct HeadSel {
+  int hb, off, hs;
+  __device__ __forceinline__ int head(int j) const { return (j / hs) * hb + off + j % hs; }
+};
+
 // Per-(batch, head) absmax of x [B, S, H, D] (element strides sb/ss/sh, D
-// contiguous): one CTA per (256-row chunk, h, b), CTA max folded into
-// amax[b*H+h] with an integer atomicMax (non-negative floats order like their
-// bit patterns; amax starts at 0).
+// contiguous) over the selected heads: one CTA per (256-row chunk, j, b),
+// CTA max folded into amax[b*nsel+j] with an integer atomicMax (non-negative
+// floats order like their bit patterns; amax starts at 0).
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads) bh_absmax_kernel(const T* __restrict__ x, long long sb, long long ss,
-                                                            long long sh, int S, int H, float* __restrict__ amax) {
+                                                            long long sh, int S, HeadSel sel, float* __restrict__ amax) {
   constexpr int CG = D / 8;
   constexpr int RL = kThreads / CG;
   __shared__ float red[kThreads / 32];
-  const int h = blockIdx.y, b = blockIdx.z;
+  const int j = blockIdx.y, b = blockIdx.z;
+  const int h = sel.head(j);
   const int cg = threadIdx.x % CG, rl = threadIdx.x / CG;
   const T* xp = x + b * sb + h * sh + cg * 8;
   const int r0 = blockIdx.x * kStatRows;
@@ -335,35 +344,37 @@ __global__ void __launch_bounds__(kThreads) bh_absmax_kernel(const T* __restrict
     for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
   }
   m = block_max(m, red);
-  if (threadIdx.x == 0) atomicMax(reinterpret_cast<int*>(amax) + (long long)b * H + h, __float_as_int(m));
+  if (threadIdx.x == 0) atomicMax(reinterpret_cast<int*>(amax) + (long long)b * gridDim.y + j, __float_as_int(m));
 }
 
-// y = x / scale[b,h] (IEEE division), e4m3 (clamped to +-448, RNE) or f16
-// (RNE), written head-group-major: out [P, B, S, H/P, D] with head h going to
-// group p = h / (H/P) - the send layout of a head-parallel all-to-all (P = 1:
-// plain [B, S, H, D]).  One thread per 8 channels.
+// y = x / scale[b, j] (IEEE division) for the selected heads, e4m3 (clamped
+// to +-448, RNE) or f16 (RNE), written block-major: out [P, B, S, hs, D] with
+// P = H/hb and selected head j = p*hs + i at [p, b, s, i] - the send buffer of
+// a head-parallel all-to-all (all heads, hb = H: plain [B, S, H, D]).  One
+// thread per 8 channels.
 template <typename T, bool OUT_F16>
 __global__ void __launch_bounds__(kThreads) bh_quant_kernel(const T* __restrict__ x, long long sb, long long ss,
-                                                           long long sh, int B, int S, int H, int D, int P,
+                                                           long long sh, int B, int S, int H, int D, HeadSel sel,
                                                            const float* __restrict__ scale, uint8_t* __restrict__ out) {
   const int CG = D / 8;
-  const int Hl = H / P;
-  const long long n = (long long)B * S * H * CG;
+  const int nsel = (H / sel.hb) * sel.hs;
+  const long long n = (long long)B * S * nsel * CG;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const int g = (int)(i % CG);
     long long t = i / CG;
-    const int h = (int)(t % H);
-    t /= H;
+    const int j = (int)(t % nsel);
+    t /= nsel;
     const int s = (int)(t % S);
     const int b = (int)(t / S);
+    const int h = sel.head(j);
     float v[8];
     load8(x + b * sb + (long long)s * ss + h * sh + g * 8, v);
-    const float sc = __ldg(scale + (long long)b * H + h);
+    const float sc = __ldg(scale + (long long)b * nsel + j);
     float y[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) y[k] = OUT_F16 ? __fdiv_rn(v[k], sc) : clamp448(__fdiv_rn(v[k], sc));
-    const int p = h / Hl, hl = h - p * Hl;
-    const long long o = ((((long long)p * B + b) * S + s) * Hl + hl) * D + g * 8;
+    const int p = j / sel.hs, hl = j - p * sel.hs;
+    const long long o = ((((long long)p * B + b) * S + s) * sel.hs + hl) * D + g * 8;
     if constexpr (OUT_F16) {
       uint4 u;
       u.x = cvt_f16x2(y[1], y[0]);
@@ -396,17 +407,22 @@ bool bh_shape_ok(const void* x, int32_t in_dtype, int64_t B, int64_t S, int64_t 
 }  // namespace
 
 extern "C" int mh3_absmax_bh(const void* x, int32_t in_dtype, int64_t B, int64_t S, int64_t H, int64_t D, int64_t sb,
-                             int64_t ss, int64_t sh, float* amax, void* stream) {
+                             int64_t ss, int64_t sh, int32_t head_block, int32_t head_off, int32_t heads_sel,
+                             float* amax, void* stream) {
   const char* why = nullptr;
   if (!bh_shape_ok(x, in_dtype, B, S, H, D, sb, ss, sh, &why)) return fail(MH3_ERR_INVALID, (std::string("mh3_absmax_bh: ") + why).c_str());
   if (amax == nullptr) return fail(MH3_ERR_INVALID, "mh3_absmax_bh: null amax");
+  if (head_block <= 0 || H % head_block || head_off < 0 || heads_sel <= 0 || head_off + heads_sel > head_block)
+    return fail(MH3_ERR_INVALID, "mh3_absmax_bh: bad head selection");
+  const quant::HeadSel sel{head_block, head_off, heads_sel};
+  const int64_t nsel = (H / head_block) * heads_sel;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemsetAsync(amax, 0, (size_t)(B * H) * sizeof(float), st);
+  cudaError_t e = cudaMemsetAsync(amax, 0, (size_t)(B * nsel) * sizeof(float), st);
   if (e != cudaSuccess) return fail_cuda(e, "mh3_absmax_bh memset");
-  const dim3 grid((unsigned)((S + quant::kStatRows - 1) / quant::kStatRows), (unsigned)H, (unsigned)B);
+  const dim3 grid((unsigned)((S + quant::kStatRows - 1) / quant::kStatRows), (unsigned)nsel, (unsigned)B);
   if (grid.x > 2147483647u) return fail(MH3_ERR_TOO_LARGE, "mh3_absmax_bh: too many rows");
 #define MH3_ABSMAX(T, DD) \
-  quant::bh_absmax_kernel<T, DD><<<grid, quant::kThreads, 0, st>>>(static_cast<const T*>(x), sb, ss, sh, (int)S, (int)H, amax)
+  quant::bh_absmax_kernel<T, DD><<<grid, quant::kThreads, 0, st>>>(static_cast<const T*>(x), sb, ss, sh, (int)S, sel, amax)
   if (in_dtype == MH3_DTYPE_BF16) {
     if (D == 128) MH3_ABSMAX(__nv_bfloat16, 128); else MH3_ABSMAX(__nv_bfloat16, 64);
   } else {
@@ -418,22 +434,24 @@ extern "C" int mh3_absmax_bh(const void* x, int32_t in_dtype, int64_t B, int64_t
 }
 
 extern "C" int mh3_quantize_bh(const void* x, int32_t in_dtype, int64_t B, int64_t S, int64_t H, int64_t D, int64_t sb,
-                               int64_t ss, int64_t sh, const float* scale, int32_t out_dtype, int32_t groups, void* out,
-                               void* stream) {
+                               int64_t ss, int64_t sh, int32_t head_block, int32_t head_off, int32_t heads_sel,
+                               const float* scale, int32_t out_dtype, void* out, void* stream) {
   const char* why = nullptr;
   if (!bh_shape_ok(x, in_dtype, B, S, H, D, sb, ss, sh, &why)) return fail(MH3_ERR_INVALID, (std::string("mh3_quantize_bh: ") + why).c_str());
   if (scale == nullptr || out == nullptr) return fail(MH3_ERR_INVALID, "mh3_quantize_bh: null scale or out");
   if (out_dtype != MH3_DTYPE_E4M3 && out_dtype != MH3_DTYPE_F16)
     return fail(MH3_ERR_INVALID, "mh3_quantize_bh: out_dtype must be e4m3 or f16");
-  if (groups <= 0 || H % groups) return fail(MH3_ERR_INVALID, "mh3_quantize_bh: groups must divide heads");
+  if (head_block <= 0 || H % head_block || head_off < 0 || heads_sel <= 0 || head_off + heads_sel > head_block)
+    return fail(MH3_ERR_INVALID, "mh3_quantize_bh: bad head selection");
+  const quant::HeadSel sel{head_block, head_off, heads_sel};
   if ((uintptr_t)out & 15u) return fail(MH3_ERR_INVALID, "mh3_quantize_bh: out must be 16-byte aligned");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const long long n = B * S * H * (D / 8);
+  const long long n = B * S * (H / head_block) * heads_sel * (D / 8);
   const int blocks = (int)std::min<long long>((n + quant::kThreads - 1) / quant::kThreads, 148ll * 16);
   uint8_t* o = static_cast<uint8_t*>(out);
 #define MH3_BHQ(T, F16)                                                                                            \
   quant::bh_quant_kernel<T, F16><<<blocks, quant::kThreads, 0, st>>>(static_cast<const T*>(x), sb, ss, sh, (int)B, \
-                                                                      (int)S, (int)H, (int)D, groups, scale, o)
+                                                                      (int)S, (int)H, (int)D, sel, scale, o)
   const bool f16 = out_dtype == MH3_DTYPE_F16;
   if (in_dtype == MH3_DTYPE_BF16) {
     if (f16) MH3_BHQ(__nv_bfloat16, true); else MH3_BHQ(__nv_bfloat16, false);

@@ -339,39 +339,51 @@ def _bh_args(x: torch.Tensor):
     return x, (x.data_ptr(), _dtype_code(x.dtype), B, S, H, D, x.stride(0), x.stride(1), x.stride(2))
 
 
-def absmax_bh(x: torch.Tensor) -> torch.Tensor:
-    """max |x[b, :, h, :]| as float32 [B, H] for x [B, S, H, D] (``mh3_absmax_bh``)."""
+def _head_sel(H: int, groups: int, head_off: int, heads_sel: int | None):
+    if groups <= 0 or H % groups:
+        raise ValueError("groups must divide the head count")
+    hb = H // groups
+    hs = hb - head_off if heads_sel is None else heads_sel
+    if head_off < 0 or hs <= 0 or head_off + hs > hb:
+        raise ValueError("bad head selection")
+    return hb, head_off, hs
+
+
+def absmax_bh(x: torch.Tensor, groups: int = 1, head_off: int = 0, heads_sel: int | None = None) -> torch.Tensor:
+    """max |x[b, :, h, :]| as float32 [B, groups*heads_sel] for x [B, S, H, D] over the selected
+    heads h = p*(H/groups) + head_off + i (``mh3_absmax_bh``; default: all heads, [B, H])."""
     lib = _lib.load()
     x, args = _bh_args(x)
-    out = torch.empty((x.shape[0], x.shape[2]), dtype=torch.float32, device=x.device)
+    hb, off, hs = _head_sel(x.shape[2], groups, head_off, heads_sel)
+    out = torch.empty((x.shape[0], groups * hs), dtype=torch.float32, device=x.device)
     with torch.cuda.device(x.device):
-        rc = lib.mh3_absmax_bh(*args, out.data_ptr(), _stream(x.device))
+        rc = lib.mh3_absmax_bh(*args, hb, off, hs, out.data_ptr(), _stream(x.device))
     _lib.check(rc, "mh3_absmax_bh")
     return out
 
 
 def quantize_bh(x: torch.Tensor, scale: torch.Tensor, out_dtype: torch.dtype = E4M3, groups: int = 1,
-                out: torch.Tensor | None = None) -> torch.Tensor:
-    """x [B,S,H,D] / scale[b,h] -> e4m3 (clamped to +-448) or f16, as
-    [groups, B, S, H/groups, D] (head h in group h // (H/groups)); ``mh3_quantize_bh``."""
+                out: torch.Tensor | None = None, head_off: int = 0, heads_sel: int | None = None) -> torch.Tensor:
+    """x [B,S,H,D] / scale[b, j] -> e4m3 (clamped to +-448) or f16, as [groups, B, S, heads_sel, D]
+    for the selected heads h = p*(H/groups) + head_off + i, numbered j = p*heads_sel + i
+    (``mh3_quantize_bh``; default: all heads, scale [B, H], out [groups, B, S, H/groups, D])."""
     lib = _lib.load()
     x, args = _bh_args(x)
     B, S, H, D = x.shape
     if out_dtype not in (E4M3, torch.float16):
         raise ValueError("out_dtype must be float8_e4m3fn or float16")
-    if groups <= 0 or H % groups:
-        raise ValueError("groups must divide the head count")
+    hb, off, hs = _head_sel(H, groups, head_off, heads_sel)
     scale = scale.to(device=x.device, dtype=torch.float32).contiguous()
-    if scale.numel() != B * H:
-        raise ValueError("scale must hold B*H values")
-    shape = (groups, B, S, H // groups, D)
+    if scale.numel() != B * groups * hs:
+        raise ValueError("scale must hold one value per (batch, selected head)")
+    shape = (groups, B, S, hs, D)
     if out is None:
         out = torch.empty(shape, dtype=out_dtype, device=x.device)
     elif tuple(out.shape) != shape or out.dtype != out_dtype or not out.is_contiguous():
         raise ValueError(f"out must be a contiguous {out_dtype} tensor of shape {shape}")
     code = _lib.MH3_DTYPE_F16 if out_dtype == torch.float16 else _lib.MH3_DTYPE_E4M3
     with torch.cuda.device(x.device):
-        rc = lib.mh3_quantize_bh(*args, scale.data_ptr(), code, int(groups), out.data_ptr(), _stream(x.device))
+        rc = lib.mh3_quantize_bh(*args, hb, off, hs, scale.data_ptr(), code, out.data_ptr(), _stream(x.device))
     _lib.check(rc, "mh3_quantize_bh")
     return out
 
@@ -471,3 +483,33 @@ def fp8_linear(x2d: torch.Tensor, w8: torch.Tensor, w_scale: torch.Tensor, bias,
         b2 = (B_cat / sb[:, None]).to(torch.bfloat16)
         a2 = scaled_gemm(xb, A_cat, row_scale=sa, row_scale_inv=True)
     return scaled_gemm(x8, w8, row_scale=sa, col_scale=sb, bias=bias, a2=a2, b2=b2)
+
+
+# ---------------------------------------------------------------------------
+# strided host <-> device row copies
+# ---------------------------------------------------------------------------
+
+
+def copy_rows(dst: torch.Tensor, dst_offset: int, dst_pitch: int, src: torch.Tensor, src_offset: int,
+              src_pitch: int, row_bytes: int, rows: int, stream: torch.cuda.Stream | None = None) -> None:
+    """Copy ``rows`` runs of ``row_bytes`` bytes from ``src`` (byte offset ``src_offset``, row pitch
+    ``src_pitch``) to ``dst`` (``dst_offset``, ``dst_pitch``), asynchronously on ``stream``
+    (``mh3_copy_rows``).  Both tensors contiguous; one on the GPU, the other pinned host memory or
+    the GPU.  Every byte touched must lie inside both tensors."""
+    for name, t, off, pitch in (("dst", dst, dst_offset, dst_pitch), ("src", src, src_offset, src_pitch)):
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+        if off < 0 or pitch < row_bytes or row_bytes < 0 or rows < 0:
+            raise ValueError("bad offsets, pitches or sizes")
+        if rows and off + (rows - 1) * pitch + row_bytes > t.numel() * t.element_size():
+            raise ValueError(f"copy runs past the end of {name}")
+    devs = [t.device for t in (dst, src) if t.device.type == "cuda"]
+    if not devs:
+        raise ValueError("one of dst / src must be a CUDA tensor")
+    if stream is None:
+        stream = torch.cuda.current_stream(devs[0])
+    lib = _lib.load()
+    with torch.cuda.device(devs[0]):
+        rc = lib.mh3_copy_rows(dst.data_ptr() + dst_offset, dst_pitch, src.data_ptr() + src_offset, src_pitch,
+                               row_bytes, rows, stream.cuda_stream)
+    _lib.check(rc, "mh3_copy_rows")

@@ -73,6 +73,9 @@ def _run(q, k, v, out, scale, key_mask, key_bias, hc, dev):
     s_cmp = torch.cuda.current_stream(dev)
     s_in = torch.cuda.Stream(dev)
     s_out = torch.cuda.Stream(dev)
+    # The chunk buffers may reuse memory that kernels already queued on the
+    # compute stream still read: the input stream starts after them.
+    s_in.wait_stream(s_cmp)
     km = key_mask.to(dev, non_blocking=True) if key_mask is not None else None
     kb = key_bias.to(dev, non_blocking=True) if key_bias is not None else None
     bufs = [tuple(torch.empty((1, hc, S, D), dtype=t.dtype, device=dev) for t, S in ((q, Sq), (k, Sk), (v, Sk)))

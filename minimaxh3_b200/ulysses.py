@@ -3,27 +3,44 @@
 The reference runs one GPU per container and has no sequence or head
 parallelism; BASELINE config 5 asks for S=75600 self-attention sharded over
 2/4/8 GPUs.  Each rank holds a contiguous sequence shard of q, k, v
-``[B, S_local, H, D]`` (the layout a sequence-parallel DiT block holds).  Per
-call:
+``[B, S_local, H, D]`` (the layout a sequence-parallel DiT block holds).  Rank
+r attends over heads ``[r*H/P, (r+1)*H/P)``.  The heads are processed in
+``head_groups`` groups G; group g takes local heads ``[g*Hg, (g+1)*Hg)``,
+``Hg = H/(P*G)``, i.e. global heads ``p*H/P + g*Hg + i`` of every rank block
+p.  Per group:
 
-1. per-(batch, head) absmax of the local shard (``mh3_absmax_bh``), one
-   ``all_reduce(MAX)`` of 3*B*H floats, so every rank quantises with the
-   global per-(b,h) scale (BASELINE configs 2/3/5 use per-(b,h) scales);
+1. per-(batch, head) absmax of the local shard's group heads
+   (``mh3_absmax_bh`` with a head selection) and one ``all_reduce(MAX)``, so
+   every rank quantises with the global per-(b,h) scale (BASELINE configs
+   2/3/5 use per-(b,h) scales);
 2. local e4m3 quantisation (V: f16 V/scale for the f16 PV product, or e4m3)
-   straight into the send layout ``[P, B, S_local, H/P, D]``
-   (``mh3_quantize_bh``, one read of the bf16 shard, no fp32 temporaries);
+   straight into the send layout ``[P, B, S_local, Hg, D]``
+   (``mh3_quantize_bh``, one read of the bf16 group heads, no fp32
+   temporaries);
 3. one NCCL ``all_to_all_single`` per tensor: rank r receives every rank's
-   tokens for heads ``[r*H/P, (r+1)*H/P)``; for B = 1 the receive buffer is
-   already ``[S, H/P, D]`` in global token order and the attention kernel
-   reads it in place through its strided TMA maps;
-4. local FP8 attention over H/P heads, written (B = 1: by the kernel itself,
-   through output strides) into the send buffer ``[P, B, S_local, H/P, D]``;
-5. one bf16 ``all_to_all_single`` back and a head interleave to
-   ``[B, S_local, H, D]``.
+   tokens for its Hg group heads; for B = 1 the receive buffer is already
+   ``[S, Hg, D]`` in global token order and the attention kernel reads it in
+   place through its strided TMA maps;
+4. local FP8 attention over the Hg heads, written (B = 1: by the kernel
+   itself, through output strides) into the send buffer
+   ``[P, B, S_local, Hg, D]``;
+5. one ``all_to_all_single`` back, after which the group's output lands in
+   its heads of ``[B, S_local, H, D]``.
 
-Only steps 1, 3 and 5 communicate; the e4m3 all-to-all moves half the bytes
-of a bf16 one.  Cross-attention to replicated text K/V needs no collective:
-call ``fp8_attention`` on the local query shard.
+Steps 1, 3 and 5 communicate (the e4m3 all-to-all moves half the bytes of a
+bf16 one).  The groups form a software pipeline: the collectives run on
+NCCL's stream asynchronously, and the host issues group g+2's absmax +
+all-reduce, group g+1's quantisation + all-to-all and group g's attention +
+all-to-all back before it waits on anything of group g-1, so the exchanges of
+neighbouring groups overlap the attention kernel.  Every quantity is per
+(batch, head), so the result is the same, bit for bit, for every G.
+
+``ulysses_attention_host`` runs the same pipeline on shards in pinned host
+memory: each group's heads are copied in (one strided copy per tensor) on
+one stream and copied back on another, overlapping the other groups'
+compute; it optionally computes the block's cross-attention to replicated
+text K/V per group as well.  Cross-attention alone needs no collective: call
+``fp8_attention`` on the local query shard.
 
 ``attn_fn``, ``absmax_fn`` and ``quant_fn`` are injectable so the collective
 plumbing can be tested on CPU ``gloo`` ranks with the oracle standing in for
@@ -44,6 +61,20 @@ def _world(group):
     return dist.get_world_size(group), dist.get_rank(group)
 
 
+def _cuda_absmax(x, groups=1, head_off=0, heads_sel=None):
+    """[B, groups*heads_sel] per-(b, selected head) absmax: ``mh3_absmax_bh``."""
+    from . import ops
+
+    return ops.absmax_bh(x, groups=groups, head_off=head_off, heads_sel=heads_sel)
+
+
+def _cuda_quant(x, scale, P, out_dtype, head_off=0, heads_sel=None):
+    """x [B,S_l,H,D] / scale[B, P*hs] -> [P, B, S_l, hs, D] (e4m3 clamp or f16): ``mh3_quantize_bh``."""
+    from . import ops
+
+    return ops.quantize_bh(x, scale, out_dtype=out_dtype, groups=P, head_off=head_off, heads_sel=heads_sel)
+
+
 def global_absmax(xs, group=None, absmax_fn=None):
     """[len(xs), B, H] float32 absmax over (S, D) of each [B,S_local,H,D], max-reduced over ranks."""
     fn = absmax_fn or _cuda_absmax
@@ -52,34 +83,20 @@ def global_absmax(xs, group=None, absmax_fn=None):
     return local
 
 
-def _cuda_absmax(x):
-    from . import ops
-
-    return ops.absmax_bh(x)
-
-
-def _cuda_quant(x, scale, P, out_dtype):
-    """x [B,S_l,H,D] / scale[B,H] -> [P, B, S_l, H/P, D] (e4m3 clamp or f16): ``mh3_quantize_bh``."""
-    from . import ops
-
-    return ops.quantize_bh(x, scale, out_dtype=out_dtype, groups=P)
-
-
-def _exchange(send, group, recv=None):
-    """all_to_all_single on the leading (rank) dimension; dtype-agnostic."""
-    recv = torch.empty_like(send) if recv is None else recv
+def _exchange_async(send, group):
+    """all_to_all_single on the leading (rank) dimension, dtype-agnostic; returns (recv, work)."""
+    recv = torch.empty_like(send)
     s8 = send.view(torch.uint8) if send.dtype == E4M3 else send
     r8 = recv.view(torch.uint8) if recv.dtype == E4M3 else recv
-    dist.all_to_all_single(r8, s8, group=group)
-    return recv
+    return recv, dist.all_to_all_single(r8, s8, group=group, async_op=True)
 
 
 def _head_major(recv):
-    """[P(src), B, S_l, Hl, D] -> [B, Hl, S, D] view (copy only when B > 1)."""
-    P, B, S_l, Hl, D = recv.shape
+    """[P(src), B, S_l, Hg, D] -> [B, Hg, S, D] view (copy only when B > 1)."""
+    P, B, S_l, Hg, D = recv.shape
     if B == 1:
-        return recv.view(P * S_l, Hl, D).permute(1, 0, 2).unsqueeze(0)  # strided, no copy
-    return recv.permute(1, 3, 0, 2, 4).reshape(B, Hl, P * S_l, D)
+        return recv.view(P * S_l, Hg, D).permute(1, 0, 2).unsqueeze(0)  # strided, no copy
+    return recv.permute(1, 3, 0, 2, 4).reshape(B, Hg, P * S_l, D)
 
 
 def _default_attn(q8, k8, v, sq, sk, sv, logit_scale_log2, out=None):
@@ -88,51 +105,251 @@ def _default_attn(q8, k8, v, sq, sk, sv, logit_scale_log2, out=None):
     return ops.attention_e4m3(q8, k8, v, sq, sk, sv, logit_scale_log2=logit_scale_log2, out=out)
 
 
+def default_head_groups(local_heads: int) -> int:
+    """Head groups of ``ulysses_attention_host``: groups of 2 heads (1 when the count is odd).
+
+    The host copies are the bound there (about 55 GB/s host->device and 33 GB/s back per
+    B200, 25 GB/s each way when both run), so the first group's input copy and the last
+    group's output copy, which nothing overlaps, should be small; a 2-head group's attention
+    launch still fills every SM several times at S >= 32K.  Device-resident calls default to
+    one group: there the all-to-alls cannot overlap the attention kernel, which holds every
+    SM, and smaller launches only add collective latency (measured at 2 GPUs, S=75600, H=40:
+    step 46.5 ms with 1 group, 50.1 ms with 10)."""
+    return local_heads // 2 if local_heads % 2 == 0 else local_heads
+
+
+def _check_heads(H, P, G):
+    if H % P:
+        raise ValueError(f"heads ({H}) must be divisible by the world size ({P})")
+    if G <= 0 or (H // P) % G:
+        raise ValueError(f"head_groups ({G}) must divide the heads per rank ({H // P})")
+
+
+class _Pipeline:
+    """The per-group stages of one Ulysses call and their issue order.
+
+    ``source(g)`` returns the group's tensors ``(q, k, v)`` [B, S_l, H', D] and
+    the head offset of the group inside each rank block of H' (the group's
+    heads are ``p*H'/P + off + i``, i < Hg); ``sink(g, recv_o, work, send_o)``
+    takes the group's output ``[P(src heads), B, S_l, Hg, D]`` once ``work``
+    (its all-to-all back, which reads ``send_o``) is waited on.  Tensors an
+    exchange touches are only freed after a stream that waited on it: the
+    sink records ``recv_o`` / ``send_o`` on its own stream when that is not
+    the compute stream.
+    """
+
+    def __init__(self, P, r, Hg, shape, out_dtype, group, pv_dtype, ls2, attn_fn, absmax_fn, quant_fn, events):
+        self.P, self.r, self.Hg = P, r, Hg
+        self.B, self.S_l, self.D = shape
+        self.out_dtype, self.group, self.pv_dtype, self.ls2 = out_dtype, group, pv_dtype, ls2
+        self.attn = attn_fn or _default_attn
+        self.direct = attn_fn is None and self.B == 1
+        self.absmax_fn = absmax_fn or _cuda_absmax
+        self.quant_fn = quant_fn or _cuda_quant
+        self.events = events
+
+    def absmax(self, xs, off):
+        local = torch.stack([self.absmax_fn(x, groups=self.P, head_off=off, heads_sel=self.Hg) for x in xs])
+        work = dist.all_reduce(local, op=dist.ReduceOp.MAX, group=self.group, async_op=True)
+        return local, work
+
+    def exchange_in(self, xs, off, amax, work):
+        work.wait()
+        scales = torch.clamp(amax, min=1e-12) / 448.0          # [3, B, P*Hg]
+        recvs, works = [], []
+        for x, s, dt in zip(xs, scales, (E4M3, E4M3, self.pv_dtype)):
+            send = self.quant_fn(x, s, self.P, dt, head_off=off, heads_sel=self.Hg)
+            recv, w = _exchange_async(send, self.group)
+            recvs.append(recv)
+            works.append((w, send))                             # send stays alive until the wait
+        return recvs, works, scales
+
+    def attend(self, recvs, works, scales):
+        for w, _ in works:
+            w.wait()
+        P, B, S_l, Hg, D = self.P, self.B, self.S_l, self.Hg, self.D
+        mine = slice(self.r * Hg, (self.r + 1) * Hg)
+        sq, sk, sv = (s[:, mine].contiguous()[..., None] for s in scales)  # [B, Hg, 1] per-(b,h)
+        hq, hk, hv = (_head_major(t) for t in recvs)
+        send_o = torch.empty((P, B, S_l, Hg, D), dtype=self.out_dtype, device=recvs[0].device)
+        ev = None
+        if self.events is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+        if self.direct:
+            # token s of group head h sits at s*Hg*D + h*D of the send buffer
+            self.attn(hq, hk, hv, sq, sk, sv, self.ls2, out=send_o.view(P * S_l, Hg, D).permute(1, 0, 2).unsqueeze(0))
+        else:
+            o = self.attn(hq, hk, hv, sq, sk, sv, self.ls2)     # [B, Hg, S, D]
+        if ev is not None:
+            ev[1].record()
+            self.events.append(ev)
+        if not self.direct:
+            # chunk p = tokens of rank p -> [P, B, S_l, Hg, D]
+            send_o.copy_(o.to(self.out_dtype).permute(2, 0, 1, 3).reshape(P, S_l, B, Hg, D).permute(0, 2, 1, 3, 4))
+        recv_o, w = _exchange_async(send_o, self.group)
+        return recv_o, (w, send_o)
+
+    def run(self, G, source, sink):
+        a, b, c = {}, {}, {}
+
+        def stage_a(g):
+            xs, off = source(g)
+            a[g] = (xs, off) + self.absmax(xs, off)
+
+        def stage_b(g):
+            b[g] = self.exchange_in(*a.pop(g))
+
+        def stage_c(g):
+            c[g] = self.attend(*b.pop(g))
+
+        def stage_d(g):
+            recv_o, (w, send_o) = c.pop(g)
+            sink(g, recv_o, w, send_o)
+
+        # Every rank issues the same collectives in the same order: all-reduce(g+2),
+        # all-to-all(g+1), all-to-all back(g) per iteration.
+        stage_a(0)
+        if G > 1:
+            stage_a(1)
+        stage_b(0)
+        for g in range(G):
+            if g + 2 < G:
+                stage_a(g + 2)
+            if g + 1 < G:
+                stage_b(g + 1)
+            stage_c(g)
+            if g >= 1:
+                stage_d(g - 1)
+        stage_d(G - 1)
+
+
 def ulysses_attention(q, k, v, group=None, scale=None, pv_dtype=torch.float16, attn_fn=None, events=None,
-                      absmax_fn=None, quant_fn=None):
+                      absmax_fn=None, quant_fn=None, head_groups=1, out=None):
     """Head-parallel FP8 attention of sequence shards ``[B, S_local, H, D]``.
 
-    Returns the local output shard ``[B, S_local, H, D]`` (bf16, like q's
-    dtype).  H must be divisible by the world size; every rank must hold the
-    same S_local.  ``events``: optional (start, end) CUDA events recorded
-    around the local attention kernel.  ``attn_fn`` / ``absmax_fn`` /
-    ``quant_fn`` replace the CUDA kernels (for CPU process groups in tests).
+    Returns the local output shard ``[B, S_local, H, D]`` (q's dtype; written
+    into ``out`` when given, contiguous).  H must be divisible by the world
+    size P and H/P by ``head_groups``; every rank must hold the same S_local.
+    ``events``: optional list that receives one (start, end) pair of timing
+    CUDA events around each local attention launch.  ``attn_fn`` /
+    ``absmax_fn`` / ``quant_fn`` replace the CUDA kernels (for CPU process
+    groups in tests; absmax_fn / quant_fn take the head selection of
+    ``ops.absmax_bh`` / ``ops.quantize_bh``).
     """
     P, r = _world(group)
     B, S_l, H, D = q.shape
-    if H % P:
-        raise ValueError(f"heads ({H}) must be divisible by the world size ({P})")
+    _check_heads(H, P, head_groups)
     Hl = H // P
-    quant = quant_fn or _cuda_quant
-    amax = global_absmax((q, k, v), group, absmax_fn)       # [3, B, H]
-    scales = torch.clamp(amax, min=1e-12) / 448.0
-    sq_full, sk_full, sv_full = scales[0], scales[1], scales[2]
-    send_q = quant(q, sq_full, P, E4M3)
-    send_k = quant(k, sk_full, P, E4M3)
-    send_v = quant(v, sv_full, P, pv_dtype)
-    recv_q, recv_k, recv_v = (_exchange(t, group) for t in (send_q, send_k, send_v))
-    hs = slice(r * Hl, (r + 1) * Hl)
-    sq = sq_full[:, hs].contiguous()[..., None]            # [B, Hl, 1] per-(b,h)
-    sk = sk_full[:, hs].contiguous()[..., None]
-    sv = sv_full[:, hs].contiguous()[..., None]
+    Hg = Hl // head_groups
+    if out is None:
+        out = torch.empty((B, S_l, H, D), dtype=q.dtype, device=q.device)
+    elif tuple(out.shape) != (B, S_l, H, D) or out.dtype != q.dtype or not out.is_contiguous():
+        raise ValueError("out must be a contiguous tensor shaped and typed like q")
+    oview = out.view(B, S_l, P, Hl, D)
     ls2 = (scale if scale is not None else 1.0 / math.sqrt(D)) * LOG2E
-    fn = attn_fn or _default_attn
-    hq, hk, hv = _head_major(recv_q), _head_major(recv_k), _head_major(recv_v)
-    # The send buffer of the way back is [P, B, S_l, Hl, D]; for B = 1 the
-    # kernel writes it directly through strides (token s of head h at
-    # s*Hl*D + h*D).
-    send_o = torch.empty((P, B, S_l, Hl, D), dtype=q.dtype, device=q.device)
-    direct = B == 1 and attn_fn is None
-    if events is not None:
-        events[0].record()
-    if direct:
-        fn(hq, hk, hv, sq, sk, sv, ls2, out=send_o.view(P * S_l, Hl, D).permute(1, 0, 2).unsqueeze(0))
-    else:
-        o = fn(hq, hk, hv, sq, sk, sv, ls2)  # [B,Hl,S,D]
-    if events is not None:
-        events[1].record()
-    if not direct:
-        # chunk p = tokens of rank p -> [P, B, S_l, Hl, D]
-        send_o.copy_(o.to(q.dtype).permute(2, 0, 1, 3).reshape(P, S_l, B, Hl, D).permute(0, 2, 1, 3, 4))
-    recv_o = _exchange(send_o, group)                       # [P(src heads), B, S_l, Hl, D]
-    return recv_o.permute(1, 2, 0, 3, 4).reshape(B, S_l, H, D)
+
+    def source(g):
+        return (q, k, v), g * Hg
+
+    def sink(g, recv_o, work, send_o):
+        work.wait()
+        oview[:, :, :, g * Hg:(g + 1) * Hg].copy_(recv_o.permute(1, 2, 0, 3, 4))
+
+    pipe = _Pipeline(P, r, Hg, (B, S_l, D), q.dtype, group, pv_dtype, ls2, attn_fn, absmax_fn, quant_fn, events)
+    pipe.run(head_groups, source, sink)
+    return out
+
+
+def ulysses_attention_host(q, k, v, out=None, group=None, scale=None, pv_dtype=torch.float16, head_groups=None,
+                           cross_kv=None, cross_out=None, events=None):
+    """``ulysses_attention`` of host-resident shards, streamed per head group.
+
+    q, k, v: contiguous pinned CPU tensors ``[B, S_local, H, D]`` (bf16 or
+    f16); ``out``: pinned CPU tensor like q (allocated when None).  The work
+    runs on the current CUDA device's current stream, which is made to wait
+    for the last copy back: ``out`` is valid once that stream is
+    synchronised.  Group g's heads (``p*H/P + g*Hg + i``) are copied to the
+    device as ``[B, S_local, P*Hg, D]`` on an input stream while earlier
+    groups compute, and its output is copied back on an output stream.
+
+    ``cross_kv``: optional (k_text, v_text) CUDA tensors ``[B, H, T, D]``
+    replicated on every rank; then each group also runs ``fp8_attention`` of
+    its query heads against them, written to ``cross_out`` (pinned CPU
+    ``[B, S_local, H, D]``, allocated when None).  Returns ``out`` or
+    ``(out, cross_out)``.
+    """
+    from . import ops
+
+    P, r = _world(group)
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if t.device.type != "cpu" or t.dim() != 4 or not t.is_contiguous() or t.shape != q.shape or t.dtype != q.dtype:
+            raise ValueError(f"{name} must be a contiguous 4-D CPU tensor shaped and typed like q")
+    B, S_l, H, D = q.shape
+    G = head_groups or default_head_groups(H // P if H % P == 0 else 1)
+    _check_heads(H, P, G)
+    Hl = H // P
+    Hg = Hl // G
+    es = q.element_size()
+    dev = torch.device("cuda", torch.cuda.current_device())
+
+    def host_like(t, name):
+        if t is None:
+            return torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+        if t.shape != q.shape or t.dtype != q.dtype or t.device.type != "cpu" or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous CPU tensor shaped like q")
+        return t
+
+    out = host_like(out, "out")
+    if cross_kv is not None:
+        cross_out = host_like(cross_out, "cross_out")
+        kt, vt = cross_kv
+        heads = [torch.tensor([p * Hl + g * Hg + i for p in range(P) for i in range(Hg)], device=dev)
+                 for g in range(G)]
+    ls2 = (scale if scale is not None else 1.0 / math.sqrt(D)) * LOG2E
+    s_cmp = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    # The device buffers below may reuse memory that kernels already queued on
+    # the compute stream still read: the input stream starts after them.
+    s_in.wait_stream(s_cmp)
+    xs = [torch.empty((G, B, S_l, P * Hg, D), dtype=q.dtype, device=dev) for _ in range(3)]
+    row = Hg * D * es                       # bytes of one group's heads of one (token, rank block)
+    pitch = Hl * D * es                     # one rank block of heads
+
+    def source(g):
+        with torch.cuda.stream(s_in):
+            for x, h in zip(xs, (q, k, v)):
+                ops.copy_rows(x[g], 0, row, h, g * row, pitch, row, B * S_l * P, stream=s_in)
+            ev = torch.cuda.Event()
+            ev.record(s_in)
+        s_cmp.wait_event(ev)
+        grp = tuple(x[g] for x in xs)
+        if cross_kv is not None:
+            from .kernels.fp8_attention import fp8_attention
+
+            c = fp8_attention(grp[0].transpose(1, 2), kt.index_select(1, heads[g]), vt.index_select(1, heads[g]),
+                              scale=scale)
+            ct = c.transpose(1, 2)          # storage is [B, S_l, P*Hg, D] (empty_like of q's view)
+            if not ct.is_contiguous():
+                ct = ct.contiguous()
+            done = torch.cuda.Event()
+            done.record(s_cmp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done)
+                ops.copy_rows(cross_out, g * row, pitch, ct, 0, row, row, B * S_l * P, stream=s_out)
+            ct.record_stream(s_out)
+        return grp, 0
+
+    def sink(g, recv_o, work, send_o):
+        with torch.cuda.stream(s_out):
+            work.wait()
+            for p in range(P):
+                ops.copy_rows(out, (p * Hl + g * Hg) * D * es, H * D * es, recv_o[p], 0, row, row, B * S_l,
+                              stream=s_out)
+        recv_o.record_stream(s_out)
+        send_o.record_stream(s_out)
+
+    pipe = _Pipeline(P, r, Hg, (B, S_l, D), q.dtype, group, pv_dtype, ls2, None, None, None, events)
+    pipe.run(G, source, sink)
+    s_cmp.wait_stream(s_out)
+    return out if cross_kv is None else (out, cross_out)

@@ -41,3 +41,33 @@ def test_bh_kernels_reject_bad_arguments():
         ops.quantize_bh(x, torch.ones(6, device="cuda"), groups=4)       # 4 does not divide 6
     with pytest.raises(ValueError):
         ops.absmax_bh(torch.zeros(1, 8, 6, 96, dtype=torch.bfloat16, device="cuda"))
+
+
+@pytest.mark.parametrize("B,S,H,D,P,off,hs", [(1, 1000, 8, 128, 2, 1, 2), (2, 517, 12, 64, 3, 0, 1),
+                                              (1, 300, 8, 128, 1, 3, 4), (1, 129, 4, 128, 4, 0, 1)])
+@pytest.mark.parametrize("out_dtype", [torch.float8_e4m3fn, torch.float16])
+def test_head_selection_bit_exact(B, S, H, D, P, off, hs, out_dtype):
+    """absmax_bh / quantize_bh over heads p*(H/P)+off+i equal the full-head kernels restricted to them."""
+    from minimaxh3_b200 import ops
+
+    g = torch.Generator(device="cuda").manual_seed(H * 100 + off)
+    x = torch.randn(B, H, S, D, generator=g, device="cuda").to(torch.bfloat16).permute(0, 2, 1, 3)
+    heads = [p * (H // P) + off + i for p in range(P) for i in range(hs)]
+    amax = ops.absmax_bh(x, groups=P, head_off=off, heads_sel=hs)
+    assert torch.equal(amax, x.float().abs().amax(dim=(1, 3))[:, heads])
+    scale = torch.clamp(amax, min=1e-12) / 448.0
+    got = ops.quantize_bh(x, scale, out_dtype=out_dtype, groups=P, head_off=off, heads_sel=hs)
+    ref = _restated(x[:, :, heads], scale, P, out_dtype)
+    assert got.shape == (P, B, S, hs, D)
+    bits = torch.uint8 if out_dtype != torch.float16 else torch.int16
+    assert torch.equal(got.view(bits), ref.view(bits))
+
+
+def test_head_selection_rejects_bad_ranges():
+    from minimaxh3_b200 import ops
+
+    x = torch.zeros(1, 8, 8, 128, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        ops.absmax_bh(x, groups=2, head_off=3, heads_sel=2)              # 3+2 > 4 heads per group
+    with pytest.raises(ValueError):
+        ops.quantize_bh(x, torch.ones(1, 4, device="cuda"), groups=2, head_off=0, heads_sel=3)

@@ -25,18 +25,27 @@ def _oracle_attn(q8, k8, v, sq, sk, sv, ls2):
     return OA.sdpa_dequant_oracle(qd, kd, vd, ls2, base2=True)
 
 
-def _oracle_absmax(x):
-    return x.float().abs().amax(dim=(1, 3))
+def _selected(H, groups, head_off, heads_sel):
+    """Heads p*(H/groups) + head_off + i, in the order mh3_absmax_bh / mh3_quantize_bh number them."""
+    hb = H // groups
+    hs = hb - head_off if heads_sel is None else heads_sel
+    return [p * hb + head_off + i for p in range(groups) for i in range(hs)], hs
 
 
-def _oracle_quant(x, scale, P, out_dtype):
-    """Restatement of mh3_quantize_bh: x [B,S_l,H,D] / scale[B,H] -> [P, B, S_l, H/P, D]."""
+def _oracle_absmax(x, groups=1, head_off=0, heads_sel=None):
+    heads, _ = _selected(x.shape[2], groups, head_off, heads_sel)
+    return x.float().abs().amax(dim=(1, 3))[:, heads]
+
+
+def _oracle_quant(x, scale, P, out_dtype, head_off=0, heads_sel=None):
+    """Restatement of mh3_quantize_bh: x [B,S_l,H,D] selected heads / scale[B, P*hs] -> [P, B, S_l, hs, D]."""
     B, S_l, H, D = x.shape
-    y = x.float() / scale[:, None, :, None]
+    heads, hs = _selected(H, P, head_off, heads_sel)
+    y = x[:, :, heads].float() / scale[:, None, :, None]
     if out_dtype == torch.float8_e4m3fn:
         y = torch.clamp(y, -448.0, 448.0)
     y = y.to(out_dtype)
-    return y.reshape(B, S_l, P, H // P, D).permute(2, 0, 1, 3, 4).contiguous()
+    return y.reshape(B, S_l, P, hs, D).permute(2, 0, 1, 3, 4).contiguous()
 
 
 def _free_port():
@@ -50,7 +59,7 @@ def _inputs(B, S, H, D):
     return [torch.randn(B, S, H, D, generator=g).to(torch.bfloat16) for _ in range(3)]
 
 
-def _worker(rank, world, port, B, S, H, D, pv, out_dir):
+def _worker(rank, world, port, B, S, H, D, pv, out_dir, head_groups=1):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -61,7 +70,7 @@ def _worker(rank, world, port, B, S, H, D, pv, out_dir):
         Sl = S // world
         sl = slice(rank * Sl, (rank + 1) * Sl)
         out = ulysses_attention(q[:, sl], k[:, sl], v[:, sl], pv_dtype=pv, attn_fn=_oracle_attn,
-                                absmax_fn=_oracle_absmax, quant_fn=_oracle_quant)
+                                absmax_fn=_oracle_absmax, quant_fn=_oracle_quant, head_groups=head_groups)
         torch.save(out, os.path.join(out_dir, f"out{rank}.pt"))
     finally:
         dist.destroy_process_group()
@@ -83,12 +92,16 @@ def _reference(B, S, H, D, pv):
     return o.to(torch.bfloat16).permute(0, 2, 1, 3)
 
 
-@pytest.mark.parametrize("world,pv", [(2, torch.float16), (4, torch.float8_e4m3fn)])
-def test_ulysses_matches_single_process(tmp_path, world, pv):
-    B, S, H, D = 1, 64 * world, 8, 64
+@pytest.mark.parametrize("world,pv,head_groups,B", [(2, torch.float16, 1, 1), (4, torch.float8_e4m3fn, 1, 1),
+                                                    (2, torch.float16, 4, 1), (2, torch.float16, 2, 2),
+                                                    (4, torch.float8_e4m3fn, 2, 1)])
+def test_ulysses_matches_single_process(tmp_path, world, pv, head_groups, B):
+    """Any head grouping of the pipeline gives the single-process result (every quantity is per head)."""
+    S, H, D = 64 * world, 8, 64
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, B, S, H, D, pv, str(tmp_path))) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, B, S, H, D, pv, str(tmp_path), head_groups))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -103,7 +116,7 @@ def test_ulysses_matches_single_process(tmp_path, world, pv):
 
 def test_ulysses_rejects_indivisible_heads(tmp_path):
     port = _free_port()
-    # heads=6 over 4 ranks is rejected before any collective
+    # heads=6 over 4 ranks, and 3 groups of 2 heads per rank, are rejected before any collective
     ctx = mp.get_context("spawn")
     procs = [ctx.Process(target=_bad_worker, args=(r, 4, port, str(tmp_path))) for r in range(4)]
     for p in procs:
@@ -123,5 +136,9 @@ def _bad_worker(rank, world, port, out_dir):
         x = torch.zeros(1, 8, 6, 64, dtype=torch.bfloat16)
         with pytest.raises(ValueError):
             ulysses_attention(x, x, x, attn_fn=_oracle_attn, absmax_fn=_oracle_absmax, quant_fn=_oracle_quant)
+        x = torch.zeros(1, 8, 8, 64, dtype=torch.bfloat16)             # 2 heads per rank, 3 groups
+        with pytest.raises(ValueError):
+            ulysses_attention(x, x, x, attn_fn=_oracle_attn, absmax_fn=_oracle_absmax, quant_fn=_oracle_quant,
+                              head_groups=3)
     finally:
         dist.destroy_process_group()

@@ -1,4 +1,5 @@
-"""Ulysses over NCCL on 2 GPUs: bit-identical to one GPU over the whole sequence.
+"""Ulysses over NCCL on 2 GPUs: bit-identical to one GPU over the whole sequence,
+for every head grouping of the pipeline and for the host-resident variant.
 
 Every rank quantises with the global per-(batch, head) scales, so the head
 shard each rank attends over holds exactly the bytes a single GPU would use;
@@ -42,15 +43,24 @@ def _worker(rank, world, port, shape, out_dir):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     try:
-        from minimaxh3_b200.ulysses import ulysses_attention
+        from minimaxh3_b200.kernels.fp8_attention import fp8_attention
+        from minimaxh3_b200.ulysses import ulysses_attention, ulysses_attention_host
 
         B, S, H, D = shape
         q, k, v = (t.cuda() for t in _inputs(B, S, H, D))
         Sl = S // world
         sl = slice(rank * Sl, (rank + 1) * Sl)
-        out = ulysses_attention(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous())
+        shard = [t[:, sl].contiguous() for t in (q, k, v)]
+        outs = {G: ulysses_attention(*shard, head_groups=G) for G in (1, 2, 4)}
+        # host-resident shards, with the cross-attention to replicated text K/V per head group
+        gt = torch.Generator().manual_seed(11)
+        kt, vt = (torch.randn(B, H, 256, D, generator=gt).to(torch.bfloat16).cuda() for _ in range(2))
+        hq, hk, hv = (t.cpu().pin_memory() for t in shard)
+        ho, hc = ulysses_attention_host(hq, hk, hv, head_groups=2, cross_kv=(kt, vt))
+        cross = fp8_attention(shard[0].transpose(1, 2), kt, vt).transpose(1, 2)
         torch.cuda.synchronize()
-        torch.save(out.cpu(), os.path.join(out_dir, f"out{rank}.pt"))
+        torch.save({"out": {G: o.cpu() for G, o in outs.items()}, "host": ho.clone(), "host_cross": hc.clone(),
+                    "cross": cross.cpu()}, os.path.join(out_dir, f"out{rank}.pt"))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -69,7 +79,13 @@ def test_ulysses_two_gpus_bit_identical(tmp_path):
     for p in procs:
         p.join(timeout=300)
         assert p.exitcode == 0
-    got = torch.cat([torch.load(tmp_path / f"out{r}.pt") for r in range(2)], dim=1)
+    res = [torch.load(tmp_path / f"out{r}.pt") for r in range(2)]
+    got = torch.cat([x["out"][1] for x in res], dim=1)
+    for x in res:
+        for G in (2, 4):                       # head-group pipeline: same bytes
+            assert torch.equal(x["out"][G], x["out"][1])
+        assert torch.equal(x["host"], x["out"][1])         # host-resident variant
+        assert torch.equal(x["host_cross"], x["cross"])    # its per-group cross-attention
     # one GPU, whole sequence, same global per-(b,h) scales
     q, k, v = (t.cuda() for t in _inputs(B, S, H, D))
     ops_in = []
