@@ -47,6 +47,40 @@ def test_e4m3_gemm_matches_scaled_mm_semantics(M, N, K):
     assert nbad == 0, (nbad, err)
 
 
+@pytest.mark.parametrize("M,N,K,R,bf16", [(1000, 1544, 640, 32, False), (4097, 5120, 512, 0, False),
+                                          (257, 264, 384, 16, False), (700, 768, 256, 0, True)])
+def test_cta_pair_kernel_matches_single_cta_kernel(monkeypatch, M, N, K, R, bf16):
+    """The 256x256 CTA-pair kernel and the 128x256 single-CTA kernel (MH3_GEMM_CTA_PAIR=0) agree to
+    one bf16 rounding (the same fp32 products per K step); row and column tails, LoRA K-steps and
+    bf16 operands included.  Both also meet the float64 restatement."""
+    from minimaxh3_b200 import ops
+
+    dt = torch.bfloat16 if bf16 else torch.float8_e4m3fn
+    x = _rand(11, M, K)
+    w = _rand(12, N, K, scale=0.02)
+    if bf16:
+        a, b, sa, sb = x, w, torch.rand(M) + 0.5, torch.rand(N) + 0.5
+    else:
+        a, sa = OL.quantize_rows(x)
+        b, sb = OL.quantize_rows(w)
+    bias = _rand(13, N, scale=0.01)
+    a2 = _rand(14, M, R, scale=0.1) if R else None
+    b2 = _rand(15, N, R, scale=0.1) if R else None
+    args = dict(row_scale=sa.reshape(-1).to(DEV), col_scale=sb.reshape(-1).to(DEV), bias=bias.to(DEV),
+                a2=None if a2 is None else a2.to(DEV), b2=None if b2 is None else b2.to(DEV))
+    pair = ops.scaled_gemm(a.to(dt).to(DEV), b.to(dt).to(DEV), **args).cpu()
+    monkeypatch.setenv("MH3_GEMM_CTA_PAIR", "0")
+    single = ops.scaled_gemm(a.to(dt).to(DEV), b.to(dt).to(DEV), **args).cpu()
+    nbad, err = _bf16_close(pair, single)
+    assert nbad == 0, (nbad, err)
+    acc = a.to(dt).double() @ b.to(dt).double().t()
+    if R:
+        acc = acc + a2.double() @ b2.double().t()
+    ref = acc * sa.reshape(-1, 1).double() * sb.reshape(1, -1).double() + bias.double()
+    r = OA.compare(pair.float(), ref)
+    assert r["cos"] > 0.99999 and r["max_abs"] <= 1e-2 * r["ref_absmax"], r
+
+
 def test_bf16_gemm_with_inverse_row_scale():
     from minimaxh3_b200 import ops
 
