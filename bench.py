@@ -503,7 +503,7 @@ def run_linear_workload(args):
     dev = torch.device("cuda", 0)
     stream = torch.cuda.current_stream(dev)
     g = torch.Generator(device=dev).manual_seed(0)
-    M = 32760
+    M = args.linear_rows
     xs = {}
     lines = []
     peaks = _peaks()
@@ -537,7 +537,7 @@ def run_linear_workload(args):
                       "gemm_frac_of_fp8_peak": flop / t_gemm / 1e9 / peaks["fp8_tflops"],
                       "fp8linear_forward_ms": t_fwd, "fp8linear_forward_tflops": flop / t_fwd / 1e9,
                       "reference_recipe_ms": t_ref, "reference_recipe_tflops": flop / t_ref / 1e9})
-    print(json.dumps({"workload": "config4: FP8 scaled linear M=32760 K=5120 (N 5120/15360/13824) and the MLP-down "
+    print(json.dumps({"workload": f"config4: FP8 scaled linear M={M} K=5120 (N 5120/15360/13824) and the MLP-down "
                                   "shape K=13824 N=5120, LoRA r=32", "unit": "TFLOP/s",
                       "peak": peaks, "results": lines}), flush=True)
 
@@ -674,6 +674,8 @@ def main():
                     help="attention = config 2 (the headline line); linear = config 4 measurements")
     ap.add_argument("--pv", default="f16", choices=["f16", "e4m3"],
                     help="PV product operands: f16 P/V (default, meets the tolerance) or e4m3")
+    ap.add_argument("--linear-rows", type=int, default=32760,
+                    help="linear workload: token rows M (32760 = config 4; smaller for ncu captures)")
     ap.add_argument("--head-groups", type=int, default=1,
                     help="N>1: head groups of the device-resident Ulysses pipeline (the value line)")
     ap.add_argument("--host-head-groups", type=int, default=0,

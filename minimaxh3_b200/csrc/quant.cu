@@ -264,6 +264,78 @@ __global__ void __launch_bounds__(kThreads) rows_quant_kernel(const T* __restric
   }
 }
 
+// Same quantisation with the row held in registers: 128 threads, R 16-byte
+// chunks each (rows up to 1024*R elements), so x is read from memory once;
+// the absmax, the scale and every quotient are those of rows_quant_kernel.
+constexpr int kRowThreads = 128;
+template <typename T, int R>
+__global__ void __launch_bounds__(kRowThreads) rows_quant_reg_kernel(const T* __restrict__ x, long long xs, int K,
+                                                                     uint8_t* __restrict__ x8,
+                                                                     float* __restrict__ scale) {
+  __shared__ float red[kRowThreads / 32];
+  const long long row = blockIdx.x;
+  const T* xp = x + row * xs;
+  uint4 raw[R];
+  float amax = 0.0f;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int c = (r * kRowThreads + (int)threadIdx.x) * 8;
+    if (c < K) {
+      raw[r] = __ldcs(reinterpret_cast<const uint4*>(xp + c));  // streamed: read once
+      float v[8];
+      unpack8<T>(raw[r], v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  float bm = red[0];
+#pragma unroll
+  for (int i = 1; i < kRowThreads / 32; ++i) bm = fmaxf(bm, red[i]);
+  const float s = fmaxf(bm, 1.0e-12f) / 448.0f;   // fp8_linear.py:20-21
+  if (threadIdx.x == 0) scale[row] = s;
+  uint8_t* op = x8 + row * K;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int c = (r * kRowThreads + (int)threadIdx.x) * 8;
+    if (c < K) {
+      float v[8], y[8];
+      unpack8<T>(raw[r], v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = clamp448(__fdiv_rn(v[i], s));   // :22
+      *reinterpret_cast<uint2*>(op + c) = pack8_e4m3(y);
+    }
+  }
+}
+
+template <typename T>
+static void launch_rows_quant(const T* x, long long xs, long long M, int K, uint8_t* x8, float* scale,
+                              cudaStream_t st) {
+  const int R = (K + kRowThreads * 8 - 1) / (kRowThreads * 8);
+#define MH3_ROWS_REG(RR) \
+  rows_quant_reg_kernel<T, RR><<<(unsigned)M, kRowThreads, 0, st>>>(x, xs, K, x8, scale)
+  switch (R) {
+    case 1: MH3_ROWS_REG(1); break;
+    case 2: MH3_ROWS_REG(2); break;
+    case 3: MH3_ROWS_REG(3); break;
+    case 4: MH3_ROWS_REG(4); break;
+    case 5: MH3_ROWS_REG(5); break;
+    case 6: MH3_ROWS_REG(6); break;
+    case 7: MH3_ROWS_REG(7); break;
+    case 8: MH3_ROWS_REG(8); break;
+    case 10: case 9: MH3_ROWS_REG(10); break;
+    case 12: case 11: MH3_ROWS_REG(12); break;
+    case 14: case 13: MH3_ROWS_REG(14); break;
+    case 16: case 15: MH3_ROWS_REG(16); break;
+    default:
+      rows_quant_kernel<T><<<(unsigned)M, kThreads, 0, st>>>(x, xs, K, x8, scale);
+  }
+#undef MH3_ROWS_REG
+}
+
 template <typename T, int D>
 static cudaError_t run_qkv(const mh3_qkv_quant_args* a, cudaStream_t st) {
   const int B = a->batch, H = a->heads, Sq = a->seqlen_q, Sk = a->seqlen_k;
@@ -511,12 +583,13 @@ extern "C" int mh3_quantize_rows(const void* x, int64_t x_stride, int32_t in_dty
   if (in_dtype != MH3_DTYPE_BF16 && in_dtype != MH3_DTYPE_F16)
     return fail(MH3_ERR_INVALID, "in_dtype must be bf16 or f16");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (K > 0x7fffffffLL) return fail(MH3_ERR_TOO_LARGE, "K too large");
   if (in_dtype == MH3_DTYPE_F16)
-    quant::rows_quant_kernel<__half><<<(unsigned)M, quant::kThreads, 0, st>>>(
-        static_cast<const __half*>(x), x_stride, (int)K, static_cast<uint8_t*>(x8), scale);
+    quant::launch_rows_quant<__half>(static_cast<const __half*>(x), x_stride, M, (int)K, static_cast<uint8_t*>(x8),
+                                     scale, st);
   else
-    quant::rows_quant_kernel<__nv_bfloat16><<<(unsigned)M, quant::kThreads, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(x), x_stride, (int)K, static_cast<uint8_t*>(x8), scale);
+    quant::launch_rows_quant<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(x), x_stride, M, (int)K,
+                                            static_cast<uint8_t*>(x8), scale, st);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "mh3_quantize_rows launch");
   return MH3_OK;

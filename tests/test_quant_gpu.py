@@ -63,8 +63,12 @@ def test_quantize_qkv_strided_inputs():
 
 
 @pytest.mark.parametrize("M,K,dtype", [(37, 160, torch.bfloat16), (1000, 5120, torch.bfloat16),
-                                       (3, 13824, torch.float16), (1, 8, torch.bfloat16)])
+                                       (3, 13824, torch.float16), (1, 8, torch.bfloat16),
+                                       (5, 9216, torch.bfloat16), (4, 16392, torch.bfloat16),
+                                       (2, 20000, torch.float16)])
 def test_quantize_rows_matches_oracle(M, K, dtype):
+    """Row-in-registers kernel (K <= 16384: 1-16 chunks of 1024, odd counts rounded up) and the
+    two-pass kernel (longer rows) give the oracle's bytes and scales."""
     from minimaxh3_b200 import ops
 
     x = _x(4, (M, K), dtype)
