@@ -495,7 +495,10 @@ def run_linear_workload(args):
     Reports, per N: the fused GEMM alone (e4m3 inputs resident), the whole
     FP8Linear.forward (row quantisation + LoRA-down + fused GEMM), and the
     reference's GPU recipe on the same box (our row quantisation +
-    torch._scaled_mm + the two LoRA matmuls and the add, fp8_linear.py:87-108).
+    torch._scaled_mm + the two LoRA matmuls and the add, fp8_linear.py:87-108);
+    and for an unquantised bf16 nn.Linear with the same adapter, the fused
+    bf16 GEMM (ops.linear_lora) against cuBLAS linear + LoRA matmuls + add
+    (runtime/lora.py:206-226).
     """
     from minimaxh3_b200 import ops
     from minimaxh3_b200.kernels.fp8_linear import FP8Linear
@@ -532,11 +535,24 @@ def run_linear_workload(args):
         t_ref = _time_cuda(ref_recipe, args.steps, args.warmup, stream)
         t_cub = _time_cuda(lambda: torch._scaled_mm(x8, mod.w8.t(), scale_a=sa, scale_b=mod.w_scale, bias=mod.bias,
                                                     out_dtype=torch.bfloat16), args.steps, args.warmup, stream)
+        # unquantised nn.Linear + the same adapter (runtime/lora.py:206-226): one fused bf16
+        # GEMM against the reference's cuBLAS linear + two LoRA matmuls + add
+        w16 = (torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        t_l16 = _time_cuda(lambda: ops.linear_lora(x, w16, mod.bias, [(A, Bm, 1.0)]), args.steps, args.warmup, stream)
+
+        def ref_bf16():
+            out = torch.nn.functional.linear(x, w16, mod.bias)
+            return out + ((x @ A.t()) @ Bm.t()).to(out.dtype)
+
+        t_r16 = _time_cuda(ref_bf16, args.steps, args.warmup, stream)
+        del w16
         lines.append({"N": N, "K": K, "gemm_ms": t_gemm, "gemm_tflops": flop / t_gemm / 1e9,
                       "cublas_scaled_mm_tflops": flop / t_cub / 1e9,
                       "gemm_frac_of_fp8_peak": flop / t_gemm / 1e9 / peaks["fp8_tflops"],
                       "fp8linear_forward_ms": t_fwd, "fp8linear_forward_tflops": flop / t_fwd / 1e9,
-                      "reference_recipe_ms": t_ref, "reference_recipe_tflops": flop / t_ref / 1e9})
+                      "reference_recipe_ms": t_ref, "reference_recipe_tflops": flop / t_ref / 1e9,
+                      "bf16_linear_lora_tflops": flop / t_l16 / 1e9,
+                      "bf16_reference_recipe_tflops": flop / t_r16 / 1e9})
     print(json.dumps({"workload": f"config4: FP8 scaled linear M={M} K=5120 (N 5120/15360/13824) and the MLP-down "
                                   "shape K=13824 N=5120, LoRA r=32", "unit": "TFLOP/s",
                       "peak": peaks, "results": lines}), flush=True)

@@ -5,7 +5,9 @@ Layout:
   _lib.py      ctypes binding of that ABI (include/mh3_b200.h)
   ops.py       torch-facing wrappers (pointers, strides, streams)
   kernels/     drop-in mirror of the reference's ``kernels`` package
-               (fp8_attention, attention_router, fp8_linear)
+               (fp8_attention, attention_router, fp8_linear) and the fused
+               LoRA wrapper of unquantised linears (lora)
+  streaming.py fp8_attention over host-resident tensors
   ulysses.py   head-parallel (Ulysses) sharding over NCCL
   build.py     nvcc recipe that builds libmh3_b200.so in-tree
 """

@@ -451,6 +451,24 @@ def _round_up(x: int, m: int) -> int:
     return (x + m - 1) // m * m
 
 
+def _lora_operands(adapters, N: int, K: int, device, col_scale=None):
+    """(A_cat [Rp, K] bf16, B_cat [N, Rp] bf16 = (scale*B)_cat / col_scale): the adapters
+    concatenated along the rank (padded to a multiple of 16 with zeros)."""
+    R = sum(int(A.shape[0]) for A, _, _ in adapters)
+    Rp = _round_up(max(R, 1), 16)
+    A_cat = torch.zeros((Rp, K), dtype=torch.bfloat16, device=device)
+    B_cat = torch.zeros((N, Rp), dtype=torch.float32, device=device)
+    r0 = 0
+    for A, B_, s in adapters:
+        r = int(A.shape[0])
+        A_cat[r0:r0 + r] = A.to(torch.bfloat16)
+        B_cat[:, r0:r0 + r] = B_.float() * float(s)
+        r0 += r
+    if col_scale is not None:
+        B_cat = B_cat / col_scale[:, None]
+    return A_cat, B_cat.to(torch.bfloat16)
+
+
 def fp8_linear(x2d: torch.Tensor, w8: torch.Tensor, w_scale: torch.Tensor, bias, adapters) -> torch.Tensor:
     """FP8Linear forward: per-token e4m3 activations, one fused GEMM (bf16 out).
 
@@ -470,19 +488,29 @@ def fp8_linear(x2d: torch.Tensor, w8: torch.Tensor, w_scale: torch.Tensor, bias,
     a2 = b2 = None
     if adapters:
         xb = x2d if x2d.dtype == torch.bfloat16 else x2d.to(torch.bfloat16)
-        R = sum(int(A.shape[0]) for A, _, _ in adapters)
-        Rp = _round_up(max(R, 1), 16)
-        A_cat = torch.zeros((Rp, K), dtype=torch.bfloat16, device=x2d.device)
-        B_cat = torch.zeros((N, Rp), dtype=torch.float32, device=x2d.device)
-        r0 = 0
-        for A, B_, s in adapters:
-            r = int(A.shape[0])
-            A_cat[r0:r0 + r] = A.to(torch.bfloat16)
-            B_cat[:, r0:r0 + r] = B_.float() * float(s)
-            r0 += r
-        b2 = (B_cat / sb[:, None]).to(torch.bfloat16)
+        A_cat, b2 = _lora_operands(adapters, N, K, x2d.device, col_scale=sb)
         a2 = scaled_gemm(xb, A_cat, row_scale=sa, row_scale_inv=True)
     return scaled_gemm(x8, w8, row_scale=sa, col_scale=sb, bias=bias, a2=a2, b2=b2)
+
+
+def linear_lora(x2d: torch.Tensor, weight: torch.Tensor, bias, adapters) -> torch.Tensor:
+    """bf16 ``x W^T + bias + sum_i scale_i (x A_i^T) B_i^T`` in one GEMM (bf16 out).
+
+    The unquantised ``nn.Linear`` + LoRA forward (runtime/lora.py:206-226
+    wraps ``nn.Linear.forward`` with fp8_linear.py:45-55): ``mh3_scaled_gemm``
+    on bf16 operands, the adapters' low-rank product accumulated into the same
+    TMEM accumulator as extra K-steps (a2 = x A_cat^T in bf16,
+    b2 = (scale*B)_cat), bias added in the epilogue, bf16 written once.
+    """
+    x2d = x2d.to(torch.bfloat16).contiguous()
+    M, K = x2d.shape
+    N = weight.shape[0]
+    w = weight.to(torch.bfloat16).contiguous()
+    a2 = b2 = None
+    if adapters:
+        A_cat, b2 = _lora_operands(adapters, N, K, x2d.device)
+        a2 = scaled_gemm(x2d, A_cat)
+    return scaled_gemm(x2d, w, bias=bias, a2=a2, b2=b2)
 
 
 # ---------------------------------------------------------------------------

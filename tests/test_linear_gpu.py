@@ -135,6 +135,37 @@ def test_fp8_linear_forward(M, K, N, n_adapters):
     assert r2["cos"] > 0.9999, r2
 
 
+@pytest.mark.parametrize("M,K,N,n_adapters", [(37, 160, 48, 1), (300, 1024, 512, 2), (1000, 5120, 1536, 1),
+                                              (129, 256, 264, 0)])
+def test_unquantised_linear_lora_fused(M, K, N, n_adapters):
+    """runtime/lora.py's nn.Linear + LoRA forward as one bf16 GEMM: against the float64 value of
+    x W^T + b + sum_i s_i (x A_i^T) B_i^T, and against the reference's two-step bf16 form."""
+    from minimaxh3_b200 import ops
+    from minimaxh3_b200.kernels.fp8_linear import apply_lora_adapters
+    from minimaxh3_b200.kernels.lora import attach_lora_registry
+
+    lin = _linear(9, K, N).to(DEV)
+    w, b = lin.weight.detach().cpu(), lin.bias.detach().cpu()
+    adapters = [(_rand(40 + i, 16 * (i + 1), K, scale=0.05), _rand(50 + i, N, 16 * (i + 1), scale=0.05), 0.5 + i)
+                for i in range(n_adapters)]
+    x = _rand(10, M, K)
+    exact = x.double() @ w.double().t() + b.double()
+    for A, B, s in adapters:
+        exact = exact + s * ((x.double() @ A.double().t()) @ B.double().t())
+    dev_adapters = [(A.to(DEV), B.to(DEV), s) for A, B, s in adapters]
+    got = ops.linear_lora(x.to(DEV), lin.weight, lin.bias, dev_adapters).float().cpu()
+    r = OA.compare(got, exact)
+    assert r["cos"] > 0.99999 and r["max_abs"] <= 1e-2 * max(r["ref_absmax"], 1e-3), r
+    attach_lora_registry(nn.Sequential(lin))
+    lin.adapters = dev_adapters
+    wrapped = lin(x.to(DEV)).float().cpu()                      # the wrapped forward takes the fused path
+    assert torch.equal(wrapped, got) or n_adapters == 0
+    two_step = apply_lora_adapters(x.to(DEV), torch.nn.functional.linear(x.to(DEV), lin.weight, lin.bias),
+                                   dev_adapters).float().cpu()
+    r2 = OA.compare(got, two_step)
+    assert r2["cos"] > 0.9999, r2
+
+
 def test_fp8_linear_compiles_without_graph_breaks():
     import torch._dynamo as dynamo
 
