@@ -676,6 +676,45 @@ def run_quant_workload(args):
                       "unit": "GB/s", "peak_hbm_gbs": peaks["hbm_gbs"], "results": lines}), flush=True)
 
 
+def run_step_workload(args):
+    """Step-residual cache reductions (runtime/step_cache.py:39-52; not the headline).
+
+    The per-step relative change of block 0's output plus the copy of it kept
+    for the next step, on a bf16 hidden state [1, 75600, 5120] (config 5's
+    tokens x the DiT width, 774 MB): ``ops.step_diff(copy=True)`` against the
+    reference's arithmetic (two fp32 copies, a difference, two abs, two means,
+    ``.item()``, clone).  Algorithmic bytes: h1 and h1_prev read once, h1_prev
+    written once.
+    """
+    from minimaxh3_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    h1 = torch.randn(1, 75600, 5120, generator=g, device=dev).to(torch.bfloat16)
+    prev = (h1.float() + 0.01 * torch.randn(1, 75600, 5120, generator=g, device=dev)).to(torch.bfloat16)
+    peaks = _peaks()
+
+    def fused():
+        sd, sp = ops.step_diff(h1, prev, copy=True).tolist()
+        return (sd / h1.numel()) / max(sp / h1.numel(), 1e-6)
+
+    def reference():
+        rel = torch.mean(torch.abs(h1.float() - prev.float())) / torch.clamp(torch.mean(torch.abs(prev.float())),
+                                                                            min=1e-6)
+        r = float(rel.item())
+        h1.detach().clone()          # the kept copy (step_cache.py:151)
+        return r
+
+    ms = _time_cuda(fused, args.steps, args.warmup, stream)
+    ms_ref = _time_cuda(reference, args.steps, args.warmup, stream)
+    algo = 3 * h1.numel() * 2
+    print(json.dumps({"workload": "step cache: relative change + kept copy of a bf16 [1, 75600, 5120] hidden state",
+                      "unit": "ms", "fused_ms": ms, "reference_arithmetic_ms": ms_ref, "algorithmic_bytes": algo,
+                      "fused_gbs": algo / ms / 1e6, "frac_of_hbm": algo / ms / 1e6 / peaks["hbm_gbs"],
+                      "includes": "one device->host read of the sums (the step's host sync)"}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -686,7 +725,8 @@ def main():
     ap.add_argument("--heads", type=int, default=40, help="heads (40 = config 2; fewer for ncu captures)")
     ap.add_argument("--no-extras", action="store_true",
                     help="kernel timing only (no e2e, no CPU baseline): the ncu capture command")
-    ap.add_argument("--workload", default="attention", choices=["attention", "linear", "quant", "varlen", "block"],
+    ap.add_argument("--workload", default="attention",
+                    choices=["attention", "linear", "quant", "varlen", "block", "step"],
                     help="attention = config 2 (the headline line); linear = config 4 measurements")
     ap.add_argument("--pv", default="f16", choices=["f16", "e4m3"],
                     help="PV product operands: f16 P/V (default, meets the tolerance) or e4m3")
@@ -705,6 +745,9 @@ def main():
         return
     if args.workload == "quant":
         run_quant_workload(args)
+        return
+    if args.workload == "step":
+        run_step_workload(args)
         return
     if args.workload == "varlen":
         run_varlen_workload(args)

@@ -32,7 +32,7 @@ extern "C" {
 #define MH3_API __attribute__((visibility("default")))
 #endif
 
-#define MH3_ABI_VERSION 3 /* 2: mh3_attn_args.kv_len; 3: head selection in mh3_absmax_bh / mh3_quantize_bh, mh3_copy_rows */
+#define MH3_ABI_VERSION 3 /* 2: mh3_attn_args.kv_len; 3: head selection in mh3_absmax_bh / mh3_quantize_bh, mh3_copy_rows, mh3_step_diff */
 
 #define MH3_OK 0
 #define MH3_ERR_INVALID (-1)     /* bad argument: shape, stride, alignment, null pointer */
@@ -43,6 +43,7 @@ extern "C" {
 #define MH3_DTYPE_BF16 0
 #define MH3_DTYPE_F16 1
 #define MH3_DTYPE_E4M3 2
+#define MH3_DTYPE_F32 3 /* mh3_step_diff only */
 
 /* Device-side error codes written by kernels into an ``err`` word. */
 #define MH3_DEVERR_NONE 0
@@ -285,6 +286,23 @@ MH3_API int mh3_quantize_bh(const void* x, int32_t in_dtype, int64_t B, int64_t 
  */
 MH3_API int mh3_copy_rows(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch, int64_t row_bytes,
                           int64_t rows, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Step-residual cache reductions                                           */
+/* ------------------------------------------------------------------------ */
+/*
+ * Replaces runtime/step_cache.py:39-52 (_rel_diff) and the clone of h1 that
+ * follows it (:151): one pass over n elements of h1 and prev (bf16, f16 or
+ * f32, 16-byte aligned) writes sums[0] = sum |h1 - prev| and
+ * sums[1] = sum |prev| (double, summed in a fixed order: the same bits for
+ * the same inputs), and with ``copy`` != 0 overwrites prev with h1 in the
+ * same pass.  rel = (sums[0]/n) / max(sums[1]/n, 1e-6) on the caller's
+ * side.  ``workspace``: mh3_step_diff_workspace_bytes() bytes of device
+ * memory, 16-byte aligned.
+ */
+MH3_API uint64_t mh3_step_diff_workspace_bytes(void);
+MH3_API int mh3_step_diff(const void* h1, void* prev, int32_t dtype, int64_t n, int32_t copy, double* sums,
+                          void* workspace, void* stream);
 
 #ifdef __cplusplus
 }

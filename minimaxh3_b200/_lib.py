@@ -21,6 +21,7 @@ MH3_ERR_TOO_LARGE = -4
 MH3_DTYPE_BF16 = 0
 MH3_DTYPE_F16 = 1
 MH3_DTYPE_E4M3 = 2
+MH3_DTYPE_F32 = 3
 MH3_DEVERR_WAIT_TIMEOUT = 1
 
 c_i32 = ctypes.c_int32
@@ -97,6 +98,8 @@ _SIGNATURES = {
     "mh3_quantize_bh": (c_i32, [c_ptr, c_i32, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i32, c_i32, c_i32,
                                 c_ptr, c_i32, c_ptr, c_ptr]),
     "mh3_copy_rows": (c_i32, [c_ptr, c_i64, c_ptr, c_i64, c_i64, c_i64, c_ptr]),
+    "mh3_step_diff_workspace_bytes": (c_u64, []),
+    "mh3_step_diff": (c_i32, [c_ptr, c_ptr, c_i32, c_i64, c_i32, c_ptr, c_ptr, c_ptr]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

@@ -541,3 +541,28 @@ def copy_rows(dst: torch.Tensor, dst_offset: int, dst_pitch: int, src: torch.Ten
         rc = lib.mh3_copy_rows(dst.data_ptr() + dst_offset, dst_pitch, src.data_ptr() + src_offset, src_pitch,
                                row_bytes, rows, stream.cuda_stream)
     _lib.check(rc, "mh3_copy_rows")
+
+
+# ---------------------------------------------------------------------------
+# step-residual cache reductions
+# ---------------------------------------------------------------------------
+_STEP_DT = {torch.bfloat16: _lib.MH3_DTYPE_BF16, torch.float16: _lib.MH3_DTYPE_F16, torch.float32: _lib.MH3_DTYPE_F32}
+
+
+def step_diff(h1: torch.Tensor, prev: torch.Tensor, copy: bool = False) -> torch.Tensor:
+    """float64 [2] on the device: (sum |h1 - prev|, sum |prev|) in one pass (``mh3_step_diff``);
+    with ``copy`` prev is overwritten with h1 in the same pass.  Same dtype, shape and device,
+    contiguous, 16-byte aligned."""
+    lib = _lib.load()
+    _require_cuda(h1, prev)
+    if h1.dtype != prev.dtype or h1.shape != prev.shape or h1.dtype not in _STEP_DT:
+        raise ValueError("h1 and prev must share a shape and a dtype in (bf16, f16, f32)")
+    if not (h1.is_contiguous() and prev.is_contiguous()):
+        raise ValueError("h1 and prev must be contiguous")
+    sums = torch.empty(2, dtype=torch.float64, device=h1.device)
+    ws = torch.empty(int(lib.mh3_step_diff_workspace_bytes()), dtype=torch.uint8, device=h1.device)
+    with torch.cuda.device(h1.device):
+        rc = lib.mh3_step_diff(h1.data_ptr(), prev.data_ptr(), _STEP_DT[h1.dtype], h1.numel(), 1 if copy else 0,
+                               sums.data_ptr(), ws.data_ptr(), _stream(h1.device))
+    _lib.check(rc, "mh3_step_diff")
+    return sums
