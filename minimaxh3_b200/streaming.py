@@ -7,7 +7,9 @@ the drop-in ``fp8_attention`` on each chunk and copies the result back.  The
 three stages run on three CUDA streams with two device buffers per stage, so
 the host->device copy of chunk i+1, the quantisation + attention of chunk i
 and the device->host copy of chunk i-1 overlap; a step costs about the
-slower of the PCIe transfer and the compute instead of their sum.
+slower of the PCIe transfer and the compute instead of their sum.  The
+input buffers persist across calls (per device, compute stream and shape),
+so back-to-back calls also overlap at their boundary.
 
 Every quantity of the reference's algorithm is per (batch, head): Q and K
 scales per 128-row block of one head, the K channel mean and V's per-channel
@@ -16,6 +18,8 @@ chunked result therefore equals one ``fp8_attention`` call over the whole
 tensors, bit for bit.
 """
 from __future__ import annotations
+
+import threading
 
 import torch
 
@@ -67,26 +71,46 @@ def fp8_attention_host(
     return out
 
 
+class _ChunkBuffers:
+    """Two device buffer sets (q, k, v chunks) per (device, dtype, shapes), kept across calls,
+    each with the event after the last attention that read it.  A call's first input copies
+    wait only for those events, so they overlap the previous call's last chunks; buffers that
+    came from the caching allocator instead would first have to wait for everything queued on
+    the compute stream (memory freed there may still be read)."""
+
+    _pool: dict = {}
+    _lock = threading.Lock()
+
+    @classmethod
+    def get(cls, key, make):
+        with cls._lock:
+            ent = cls._pool.get(key)
+            if ent is None:
+                ent = {"bufs": [make() for _ in range(2)], "free": [None, None]}
+                if len(cls._pool) >= 8:          # bound the cache: drop the oldest shape
+                    cls._pool.pop(next(iter(cls._pool)))
+                cls._pool[key] = ent
+            return ent
+
+
 def _run(q, k, v, out, scale, key_mask, key_bias, hc, dev):
     B, H, Sq, D = q.shape
     Sk = k.shape[2]
     s_cmp = torch.cuda.current_stream(dev)
     s_in = torch.cuda.Stream(dev)
     s_out = torch.cuda.Stream(dev)
-    # The chunk buffers may reuse memory that kernels already queued on the
-    # compute stream still read: the input stream starts after them.
-    s_in.wait_stream(s_cmp)
     km = key_mask.to(dev, non_blocking=True) if key_mask is not None else None
     kb = key_bias.to(dev, non_blocking=True) if key_bias is not None else None
-    bufs = [tuple(torch.empty((1, hc, S, D), dtype=t.dtype, device=dev) for t, S in ((q, Sq), (k, Sk), (v, Sk)))
-            for _ in range(2)]
-    ev_cmp = []
+    key = (dev.index, s_cmp.cuda_stream, q.dtype, hc, Sq, Sk, D)  # one buffer pair per compute stream
+    ent = _ChunkBuffers.get(key, lambda: tuple(torch.empty((1, hc, S, D), dtype=q.dtype, device=dev)
+                                               for S in (Sq, Sk, Sk)))
     for i, (b, h0, h1) in enumerate(_chunks(B, H, hc)):
         n = h1 - h0
-        dq, dk, dv = (x[:, :n] for x in bufs[i % 2])
+        j = i % 2
+        dq, dk, dv = (x[:, :n] for x in ent["bufs"][j])
         with torch.cuda.stream(s_in):
-            if i >= 2:
-                s_in.wait_event(ev_cmp[i - 2])  # attention i-2 has read this buffer
+            if ent["free"][j] is not None:
+                s_in.wait_event(ent["free"][j])  # the last attention that read this set is done
             dq[0].copy_(q[b, h0:h1], non_blocking=True)
             dk[0].copy_(k[b, h0:h1], non_blocking=True)
             dv[0].copy_(v[b, h0:h1], non_blocking=True)
@@ -96,12 +120,9 @@ def _run(q, k, v, out, scale, key_mask, key_bias, hc, dev):
                           key_bias=None if kb is None else kb[b:b + 1])
         ev = torch.cuda.Event()
         ev.record(s_cmp)
-        ev_cmp.append(ev)
+        ent["free"][j] = ev
         with torch.cuda.stream(s_out):
             s_out.wait_event(ev)
             out[b, h0:h1].copy_(o[0], non_blocking=True)
         o.record_stream(s_out)
-    for x in bufs:
-        for t in x:
-            t.record_stream(s_in)
     s_cmp.wait_stream(s_out)
