@@ -49,6 +49,7 @@ the kernels; the defaults are the CUDA kernels and fail loudly without them.
 from __future__ import annotations
 
 import math
+import threading
 
 import torch
 import torch.distributed as dist
@@ -190,7 +191,7 @@ class _Pipeline:
         recv_o, w = _exchange_async(send_o, self.group)
         return recv_o, (w, send_o)
 
-    def run(self, G, source, sink):
+    def run(self, G, source, sink, on_quantized=None):
         a, b, c = {}, {}, {}
 
         def stage_a(g):
@@ -199,6 +200,8 @@ class _Pipeline:
 
         def stage_b(g):
             b[g] = self.exchange_in(*a.pop(g))
+            if on_quantized is not None:
+                on_quantized(g)  # the group's inputs are no longer read
 
         def stage_c(g):
             c[g] = self.attend(*b.pop(g))
@@ -261,6 +264,23 @@ def ulysses_attention(q, k, v, group=None, scale=None, pv_dtype=torch.float16, a
     return out
 
 
+class _HostShardBuffers:
+    """Device copies of host-resident shards, reused across ``ulysses_attention_host`` calls."""
+
+    _pool: dict = {}
+    _lock = threading.Lock()
+
+    @classmethod
+    def get(cls, key, make, groups):
+        with cls._lock:
+            ent = cls._pool.get(key)
+            if ent is None:
+                if len(cls._pool) >= 4:          # bound the cache: drop the oldest shape
+                    cls._pool.pop(next(iter(cls._pool)))
+                ent = cls._pool[key] = {"bufs": make(), "free": [None] * groups}
+            return ent
+
+
 def ulysses_attention_host(q, k, v, out=None, group=None, scale=None, pv_dtype=torch.float16, head_groups=None,
                            cross_kv=None, cross_out=None, events=None):
     """``ulysses_attention`` of host-resident shards, streamed per head group.
@@ -309,15 +329,21 @@ def ulysses_attention_host(q, k, v, out=None, group=None, scale=None, pv_dtype=t
     ls2 = (scale if scale is not None else 1.0 / math.sqrt(D)) * LOG2E
     s_cmp = torch.cuda.current_stream(dev)
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    # The device buffers below may reuse memory that kernels already queued on
-    # the compute stream still read: the input stream starts after them.
-    s_in.wait_stream(s_cmp)
-    xs = [torch.empty((G, B, S_l, P * Hg, D), dtype=q.dtype, device=dev) for _ in range(3)]
+    # Device copies of the shard, kept across calls (per device, compute stream
+    # and shape): group g's buffer is refilled once the previous call's
+    # quantisation of group g (its last reader) is done, so a call's first
+    # copies overlap the previous call's last groups.
+    ent = _HostShardBuffers.get((dev.index, s_cmp.cuda_stream, q.dtype, G, B, S_l, P * Hg, D),
+                                lambda: [torch.empty((G, B, S_l, P * Hg, D), dtype=q.dtype, device=dev)
+                                         for _ in range(3)], G)
+    xs, free = ent["bufs"], ent["free"]
     row = Hg * D * es                       # bytes of one group's heads of one (token, rank block)
     pitch = Hl * D * es                     # one rank block of heads
 
     def source(g):
         with torch.cuda.stream(s_in):
+            if free[g] is not None:
+                s_in.wait_event(free[g])
             for x, h in zip(xs, (q, k, v)):
                 ops.copy_rows(x[g], 0, row, h, g * row, pitch, row, B * S_l * P, stream=s_in)
             ev = torch.cuda.Event()
@@ -349,7 +375,12 @@ def ulysses_attention_host(q, k, v, out=None, group=None, scale=None, pv_dtype=t
         recv_o.record_stream(s_out)
         send_o.record_stream(s_out)
 
+    def quantized(g):
+        ev = torch.cuda.Event()
+        ev.record(s_cmp)
+        free[g] = ev
+
     pipe = _Pipeline(P, r, Hg, (B, S_l, D), q.dtype, group, pv_dtype, ls2, None, None, None, events)
-    pipe.run(G, source, sink)
+    pipe.run(G, source, sink, on_quantized=quantized)
     s_cmp.wait_stream(s_out)
     return out if cross_kv is None else (out, cross_out)

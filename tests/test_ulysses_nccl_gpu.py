@@ -100,3 +100,47 @@ def test_ulysses_two_gpus_bit_identical(tmp_path):
     ref = ops.attention_e4m3(*ops_in, *scales, logit_scale_log2=1.4426950408889634 / math.sqrt(D))
     ref = ref.permute(0, 2, 1, 3).cpu()
     assert torch.equal(got, ref)
+
+
+def _single_rank_worker(port, out_dir):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(0)
+    dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", 0))
+    try:
+        from minimaxh3_b200.kernels.fp8_attention import fp8_attention
+        from minimaxh3_b200.ulysses import ulysses_attention, ulysses_attention_host
+
+        B, S, H, D = 1, 1000, 8, 128
+        q, k, v = (t.cuda() for t in _inputs(B, S, H, D))
+        gt = torch.Generator().manual_seed(11)
+        kt, vt = (torch.randn(B, H, 256, D, generator=gt).to(torch.bfloat16).cuda() for _ in range(2))
+        dev_out = ulysses_attention(q, k, v)
+        cross = fp8_attention(q.transpose(1, 2), kt, vt).transpose(1, 2)
+        hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+        res = []
+        for G in (4, 4, 2):                      # the second call reuses the first one's device buffers
+            o, c = ulysses_attention_host(hq, hk, hv, head_groups=G, cross_kv=(kt, vt))
+            torch.cuda.synchronize()
+            res.append((o.clone(), c.clone()))
+        torch.save({"dev": dev_out.cpu(), "cross": cross.cpu(), "host": res}, os.path.join(out_dir, "single.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_host_resident_pipeline_on_one_rank(tmp_path):
+    """ulysses_attention_host on a one-rank NCCL group equals the device path and per-group
+    cross-attention bit for bit, also when a call reuses the previous call's device buffers."""
+    ctx = mp.get_context("spawn")
+    p = ctx.Process(target=_single_rank_worker, args=(_free_port(), str(tmp_path)))
+    p.start()
+    p.join(timeout=300)
+    assert p.exitcode == 0
+    r = torch.load(tmp_path / "single.pt")
+    for o, c in r["host"]:
+        assert torch.equal(o, r["dev"])
+        assert torch.equal(c, r["cross"])
