@@ -68,8 +68,17 @@ struct __align__(1024) Smem {
   int abort_flag;
 };
 
+// TMEM per CTA: two accumulators of BN columns (rounded to the 32-column
+// allocation granule; a power of two).  The narrow tile takes 128 columns, so
+// two CTAs share an SM - the narrow GEMMs (the LoRA-down x A^T, N = rank) are
+// memory-bound and the second CTA hides load latency and the tail wave.
 template <int BN>
-__global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_constant__ Params p) {
+constexpr uint32_t kAccCols = BN <= 64 ? 64u : 256u;
+template <int BN>
+constexpr uint32_t kTmemCols = 2u * kAccCols<BN>;
+
+template <int BN>
+__global__ void __launch_bounds__(NUM_THREADS, BN == 64 ? 2 : 1) gemm_kernel(const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   Smem<BN>& sm = *reinterpret_cast<Smem<BN>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
@@ -105,7 +114,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(&sm.tmem_base), 512);
+    tmem_alloc(smem_u32(&sm.tmem_base), kTmemCols<BN>);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -162,7 +171,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
       int it = 0, tcount = 0;
       for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tcount) {
         const int acc = tcount & 1;
-        const uint32_t d_tmem = tmem + (uint32_t)(acc * 256);
+        const uint32_t d_tmem = tmem + (uint32_t)(acc * kAccCols<BN>);
         mbar_wait(smem_u32(&sm.acc_empty[acc]), ((uint32_t)(tcount >> 1) & 1u) ^ 1u, g);
         tc_fence_after();
         for (int s = 0; s < kst; ++s, ++it) {
@@ -212,7 +221,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t v[32];
-        tmem_ld32(tmem + (uint32_t)(acc * 256 + c * 32) + lane_off, v);
+        tmem_ld32(tmem + (uint32_t)(acc * kAccCols<BN> + c * 32) + lane_off, v);
         tmem_wait_ld();
         const int nc = n0 + c * 32;
         if (nc >= p.N) continue;
@@ -252,7 +261,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, kTmemCols<BN>);
   }
 }
 
@@ -614,7 +623,8 @@ static cudaError_t launch(const Params& p, cudaStream_t st) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   const long long tiles = (long long)((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
-  const int grid = (int)(tiles < nsm ? tiles : nsm);
+  const long long slots = (long long)nsm * (BN == 64 ? 2 : 1);  // resident CTAs
+  const int grid = (int)(tiles < slots ? tiles : slots);
   kern<<<grid, NUM_THREADS, smem_bytes<BN>(), st>>>(p);
   return cudaGetLastError();
 }
