@@ -1,0 +1,39 @@
+"""Host-side argument logic that needs no GPU: strided-copy bounds, head selection, head groups."""
+import pytest
+import torch
+
+from minimaxh3_b200 import ops
+from minimaxh3_b200.ulysses import _check_heads, default_head_groups
+
+
+def test_copy_rows_rejects_copies_outside_either_tensor():
+    src = torch.zeros(4 * 64, dtype=torch.uint8)
+    dst = torch.zeros(4 * 32, dtype=torch.uint8)
+    # 4 rows of 32 bytes at a 64-byte pitch fit src; 4 rows at a 40-byte pitch overrun dst
+    with pytest.raises(ValueError, match="past the end of dst"):
+        ops.copy_rows(dst, 0, 40, src, 0, 64, 32, 4)
+    with pytest.raises(ValueError, match="past the end of src"):
+        ops.copy_rows(dst, 0, 32, src, 40, 64, 32, 4)
+    with pytest.raises(ValueError, match="bad offsets"):
+        ops.copy_rows(dst, 0, 16, src, 0, 64, 32, 4)           # pitch below the row length
+    with pytest.raises(ValueError, match="contiguous"):
+        ops.copy_rows(dst, 0, 32, torch.zeros(8, 64, dtype=torch.uint8).t(), 0, 64, 32, 4)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.copy_rows(dst, 0, 32, src, 0, 64, 32, 4)           # in bounds, but neither side is on a GPU
+
+
+def test_head_selection_arithmetic():
+    assert ops._head_sel(40, 2, 0, None) == (20, 0, 20)
+    assert ops._head_sel(40, 2, 5, 5) == (20, 5, 5)
+    for args in ((40, 3, 0, None), (40, 2, 18, 5), (40, 2, -1, 2), (40, 2, 0, 0)):
+        with pytest.raises(ValueError):
+            ops._head_sel(*args)
+
+
+def test_head_groups_defaults_and_checks():
+    assert [default_head_groups(h) for h in (40, 20, 10, 5, 1)] == [20, 10, 5, 5, 1]
+    _check_heads(40, 2, 10)
+    with pytest.raises(ValueError):
+        _check_heads(40, 3, 1)
+    with pytest.raises(ValueError):
+        _check_heads(40, 2, 3)
