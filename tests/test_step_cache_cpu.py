@@ -98,3 +98,62 @@ def test_inactive_below_nine_steps_or_zero_threshold():
     assert not cache.active
     cache.begin(20, 0.5)
     assert cache.active
+
+
+class _PairBlock(nn.Module):
+    """A block whose hidden state is a (video, audio) tuple, as in joint audio-video DiTs."""
+
+    def __init__(self, i):
+        super().__init__()
+        self.i = i
+        self.calls = 0
+
+    def forward(self, x, a, temb):
+        self.calls += 1
+        f = 1.0 + 0.01 * (self.i + 1)
+        return x * f + 0.001 * temb, a * f + 0.002 * temb
+
+
+class _PairToy(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.blocks = nn.ModuleList([_PairBlock(i) for i in range(3)])
+
+    def forward(self, x, a, temb):
+        for b in self.blocks:
+            x, a = b(x, a, temb)
+        return x, a
+
+
+def test_tuple_states_follow_the_rule():
+    steps, thr = 14, 0.012
+    model = _PairToy()
+    cache = StepResidualCache().attach(model)
+    g = torch.Generator().manual_seed(1)
+    bx, ba = torch.randn(2, 16, 8, generator=g), torch.randn(2, 4, 8, generator=g)
+    cache.begin(steps, thr, warmup=3, tail=2)
+    h_prev, acc, have_res, last_res, n_skip = None, 0.0, False, None, 0
+    for s in range(steps):
+        x, a, t = bx * (1.0 + 0.002 * s), ba * (1.0 + 0.002 * s), float(s)
+        before = model.blocks[1].calls
+        ox, oa = model(x, a, t)
+        skipped = model.blocks[1].calls == before
+        h1 = (x * 1.01 + 0.001 * t, a * 1.01 + 0.002 * t)
+        if h_prev is not None:
+            rels = [float(torch.mean(torch.abs(u - v)) / torch.clamp(torch.mean(torch.abs(v)), min=1e-6))
+                    for u, v in zip(h1, h_prev)]
+            acc += sum(rels) / len(rels)
+        else:
+            acc = math.inf
+        h_prev = tuple(u.clone() for u in h1)
+        expect = 3 <= s < steps - 2 and have_res and acc < thr
+        assert skipped == expect
+        n_skip += skipped
+        if skipped:
+            assert torch.allclose(ox, h1[0] + last_res[0], atol=1e-5)
+            assert torch.allclose(oa, h1[1] + last_res[1], atol=1e-5)
+        else:
+            acc, have_res = 0.0, True
+            last_res = (ox - h1[0], oa - h1[1])
+    cache.end()
+    assert 0 < n_skip < steps
