@@ -179,7 +179,7 @@ def cpu_reference_sample(seconds: float = 10.0):
 
 
 def cpu_config1():
-    """SURVEY config 1 on the host: routed_sdpa's torch SDPA fallback, fp32
+    """Config 1 (the reference's CPU-runnable case) on the host: routed_sdpa's torch SDPA fallback, fp32
     q,k,v [1,8,1024,128] seed 0, 3 warm-ups then the median of 20."""
     import platform
     import statistics
@@ -677,7 +677,7 @@ def run_quant_workload(args):
 
 
 def run_step_workload(args):
-    """Step-residual cache reductions (runtime/step_cache.py:39-52, SURVEY §8(f) item 4; not the headline).
+    """Step-residual cache reductions (runtime/step_cache.py:39-52; not the headline).
 
     The per-step relative change of block 0's output plus the copy of it kept
     for the next step, on a bf16 hidden state [1, 75600, 5120] (config 5's
