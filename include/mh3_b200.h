@@ -32,7 +32,11 @@ extern "C" {
 #define MH3_API __attribute__((visibility("default")))
 #endif
 
-#define MH3_ABI_VERSION 3 /* 2: mh3_attn_args.kv_len; 3: head selection in mh3_absmax_bh / mh3_quantize_bh, mh3_copy_rows, mh3_step_diff */
+/* ABI history: 1: the first release, mh3_quantize_qkv_noalloc included;
+ * 2: mh3_attn_args.kv_len; 3: head selection in mh3_absmax_bh /
+ * mh3_quantize_bh, mh3_copy_rows, mh3_step_diff; 4: f32 input to
+ * mh3_quantize_rows. */
+#define MH3_ABI_VERSION 4
 
 #define MH3_OK 0
 #define MH3_ERR_INVALID (-1)     /* bad argument: shape, stride, alignment, null pointer */
@@ -43,7 +47,7 @@ extern "C" {
 #define MH3_DTYPE_BF16 0
 #define MH3_DTYPE_F16 1
 #define MH3_DTYPE_E4M3 2
-#define MH3_DTYPE_F32 3 /* mh3_step_diff only */
+#define MH3_DTYPE_F32 3 /* mh3_step_diff and mh3_quantize_rows input */
 
 /* Device-side error codes written by kernels into an ``err`` word. */
 #define MH3_DEVERR_NONE 0
@@ -188,8 +192,9 @@ MH3_API int mh3_quantize_qkv_noalloc(const mh3_qkv_quant_args* args, void* strea
 /*
  * Replaces ``_quantize_rows_kernel`` / ``quantize_rows``
  * (kernels/fp8_linear.py:8-42): x8[m,:] = e4m3(clamp(x[m,:]/s[m], +-448)),
- * s[m] = max(absmax(x[m,:]), 1e-12)/448.  x is [M,K] with row stride
- * x_stride (elements); x8 is contiguous [M,K]; scale is [M] f32.
+ * s[m] = max(absmax(x[m,:]), 1e-12)/448.  x is [M,K] bf16, f16 or f32
+ * (in_dtype; the reference's kernel loads any float dtype, :19) with row
+ * stride x_stride (elements); x8 is contiguous [M,K]; scale is [M] f32.
  */
 MH3_API int mh3_quantize_rows(const void* x, int64_t x_stride, int32_t in_dtype, int64_t M, int64_t K, void* x8,
                       float* scale, void* stream);

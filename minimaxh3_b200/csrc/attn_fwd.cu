@@ -216,11 +216,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
       // Teardown: let the last copy issued into each stage land before exit.
       const int nk_issued = issued >= 0 ? issued : -issued;
       const int nv_issued = issued >= 0 ? issued : -issued - 1;
-      mbar_wait_teardown(bq, 0, p.timeout_ns);
+      mbar_wait_teardown(bq, 0);
       for (int j = (nk_issued > KST ? nk_issued - KST : 0); j < nk_issued; ++j)
-        mbar_wait_teardown(smem_u32(&sm.bar_kfull[j % KST]), (uint32_t)(j / KST) & 1u, p.timeout_ns);
+        mbar_wait_teardown(smem_u32(&sm.bar_kfull[j % KST]), (uint32_t)(j / KST) & 1u);
       for (int j = (nv_issued > VST ? nv_issued - VST : 0); j < nv_issued; ++j)
-        mbar_wait_teardown(smem_u32(&sm.bar_vfull[j % VST]), (uint32_t)(j / VST) & 1u, p.timeout_ns);
+        mbar_wait_teardown(smem_u32(&sm.bar_vfull[j % VST]), (uint32_t)(j / VST) & 1u);
     } else if (warp == 9 && lane == 0) {
       // ---------------------------------------------------------------- MMA issuer
       constexpr uint32_t kIdescS = idesc_e4m3(BM, BN, false, false);
@@ -317,7 +317,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
       mma_commit(smem_u32(&sm.bar_o));
       (void)ok;
       // Every MMA must be finished before the CTA frees TMEM.
-      mbar_wait_teardown(smem_u32(&sm.bar_o), 0, p.timeout_ns);
+      mbar_wait_teardown(smem_u32(&sm.bar_o), 0);
     }
   } else {
     // ------------------------------------------------------------------ softmax

@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(NUM_THREADS, BN == 64 ? 2 : 1) gemm_kernel(con
       }
       // Teardown: the last copy issued into each stage must land.
       for (int i = max(0, last_issued - STAGES + 1); i <= last_issued; ++i)
-        mbar_wait_teardown(smem_u32(&sm.full[i % STAGES]), (uint32_t)(i / STAGES) & 1u, p.timeout_ns);
+        mbar_wait_teardown(smem_u32(&sm.full[i % STAGES]), (uint32_t)(i / STAGES) & 1u);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -198,7 +198,7 @@ __global__ void __launch_bounds__(NUM_THREADS, BN == 64 ? 2 : 1) gemm_kernel(con
       // Every MMA must be finished before the CTA frees TMEM (also on the
       // abort path, where the epilogue's waits return early).
       mma_commit(smem_u32(&sm.mma_done));
-      mbar_wait_teardown(smem_u32(&sm.mma_done), 0, p.timeout_ns);
+      mbar_wait_teardown(smem_u32(&sm.mma_done), 0);
     }
   } else {
     // ------------------------------------------------------------------ epilogue
@@ -433,7 +433,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_pair_kernel(const __grid_
     // Teardown (leader): the last copies counted on each stage must land.
     if (crank == 0 && lane == 0)
       for (int i = max(0, last_issued - PAIR_STAGES + 1); i <= last_issued; ++i)
-        mbar_wait_teardown(smem_u32(&sm.full[i % PAIR_STAGES]), (uint32_t)(i / PAIR_STAGES) & 1u, p.timeout_ns);
+        mbar_wait_teardown(smem_u32(&sm.full[i % PAIR_STAGES]), (uint32_t)(i / PAIR_STAGES) & 1u);
   } else if (warp == 1) {
     if (crank == 0) {
       // -------------------------------------------------------------- MMA issuer (leader)
@@ -474,7 +474,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_pair_kernel(const __grid_
     }
     // Both CTAs: every pair MMA (they write both CTAs' TMEM) must be
     // finished before TMEM is freed, also on the abort path.
-    if (lane == 0) mbar_wait_teardown(smem_u32(&sm.mma_done), 0, p.timeout_ns);
+    if (lane == 0) mbar_wait_teardown(smem_u32(&sm.mma_done), 0);
   } else {
     // ------------------------------------------------------------------ epilogue (both CTAs)
     const int q = warp & 3;                    // TMEM lane quarter of this warp

@@ -125,12 +125,20 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
   }
 }
 
+// Bound of every teardown wait.  It is independent of the caller's pipeline
+// timeout on purpose: a pipeline wait may give up after a few microseconds
+// (a short ``timeout_ns``), but TMA copies and MMAs that were already issued
+// still complete in microseconds, and the CTA must not free TMEM or exit with
+// them in flight.  Ten seconds is a bound for a broken device, not for work.
+constexpr uint64_t kTeardownWaitNs = 10ull * 1000ull * 1000ull * 1000ull;
+
 // Bounded wait that ignores the abort flag: used at teardown to let copies
-// that are still in flight land before the CTA exits.
-__device__ __forceinline__ bool mbar_wait_teardown(uint32_t bar, uint32_t parity, uint64_t timeout_ns) {
+// and MMAs that are still in flight complete before the CTA exits.
+__device__ __forceinline__ bool mbar_wait_teardown(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer_ns() - t0 > timeout_ns) return false;
+    if (globaltimer_ns() - t0 > kTeardownWaitNs) return false;
   }
   return true;
 }

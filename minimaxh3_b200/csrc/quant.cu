@@ -28,6 +28,13 @@ constexpr int kStatRows = 256;   // rows per K/V statistics chunk
 
 template <typename T>
 __device__ __forceinline__ void load8(const T* p, float (&x)[8]) {
+  if constexpr (std::is_same<T, float>::value) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *reinterpret_cast<const float4*>(p + 4);
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+    return;
+  }
   const uint4 u = *reinterpret_cast<const uint4*>(p);
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -585,11 +592,14 @@ extern "C" int mh3_quantize_rows(const void* x, int64_t x_stride, int32_t in_dty
   if (K % 8 || x_stride % 8 || ((uintptr_t)x & 15u) || ((uintptr_t)x8 & 7u))
     return fail(MH3_ERR_UNSUPPORTED, "K and the row stride must be multiples of 8, x 16-byte aligned");
   if (M > 0x7fffffffLL) return fail(MH3_ERR_TOO_LARGE, "M too large");
-  if (in_dtype != MH3_DTYPE_BF16 && in_dtype != MH3_DTYPE_F16)
-    return fail(MH3_ERR_INVALID, "in_dtype must be bf16 or f16");
+  if (in_dtype != MH3_DTYPE_BF16 && in_dtype != MH3_DTYPE_F16 && in_dtype != MH3_DTYPE_F32)
+    return fail(MH3_ERR_INVALID, "in_dtype must be bf16, f16 or f32");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (K > 0x7fffffffLL) return fail(MH3_ERR_TOO_LARGE, "K too large");
-  if (in_dtype == MH3_DTYPE_F16)
+  if (in_dtype == MH3_DTYPE_F32)  // float rows (the reference loads any float dtype, fp8_linear.py:19)
+    quant::rows_quant_kernel<float><<<(unsigned)M, quant::kThreads, 0, st>>>(static_cast<const float*>(x), x_stride,
+                                                                            (int)K, static_cast<uint8_t*>(x8), scale);
+  else if (in_dtype == MH3_DTYPE_F16)
     quant::launch_rows_quant<__half>(static_cast<const __half*>(x), x_stride, M, (int)K, static_cast<uint8_t*>(x8),
                                      scale, st);
   else

@@ -26,8 +26,9 @@ def quantize_rows(x2d: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Per-row e4m3 quantisation: (x8 [M,K], x_scale [M,1] f32).  fp8_linear.py:27-42."""
     if x2d.ndim != 2 or not x2d.is_cuda:
         raise ValueError("quantize_rows expects a 2D CUDA tensor")
-    if x2d.dtype not in (torch.bfloat16, torch.float16):
-        x2d = x2d.to(torch.bfloat16) if x2d.dtype != torch.float32 else x2d
+    if x2d.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        # the reference's kernel loads any float dtype and computes in fp32 (:19)
+        x2d = x2d.to(torch.float32)
     return _ops.quantize_rows(x2d)
 
 

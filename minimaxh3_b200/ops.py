@@ -295,10 +295,14 @@ def quantize_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_premul: fl
 
 
 def quantize_rows(x2d: torch.Tensor):
-    """Per-row e4m3 quantisation (``mh3_quantize_rows``): (x8 [M,K], scale [M,1])."""
+    """Per-row e4m3 quantisation (``mh3_quantize_rows``): (x8 [M,K], scale [M,1]).
+
+    x2d: bf16, f16 or f32 [M,K] on the device."""
     lib = _lib.load()
     if x2d.dim() != 2 or not x2d.is_cuda:
         raise ValueError("quantize_rows expects a 2D CUDA tensor")
+    if x2d.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        raise ValueError(f"quantize_rows: unsupported dtype {x2d.dtype} (bf16, f16 or f32)")
     if x2d.stride(1) != 1 or x2d.stride(0) % 8 or x2d.data_ptr() % 16:
         x2d = x2d.contiguous()
     M, K = x2d.shape
@@ -306,7 +310,8 @@ def quantize_rows(x2d: torch.Tensor):
     scale = torch.empty((M, 1), dtype=torch.float32, device=x2d.device)
     if M > 0 and K > 0:
         with torch.cuda.device(x2d.device):
-            rc = lib.mh3_quantize_rows(x2d.data_ptr(), x2d.stride(0), _dtype_code(x2d.dtype), M, K,
+            code = _lib.MH3_DTYPE_F32 if x2d.dtype == torch.float32 else _dtype_code(x2d.dtype)
+            rc = lib.mh3_quantize_rows(x2d.data_ptr(), x2d.stride(0), code, M, K,
                                        x8.data_ptr(), scale.data_ptr(), _stream(x2d.device))
         _lib.check(rc, "mh3_quantize_rows")
     return x8, scale
@@ -394,12 +399,15 @@ def quantize_bh(x: torch.Tensor, scale: torch.Tensor, out_dtype: torch.dtype = E
 
 
 def scaled_gemm(a: torch.Tensor, b: torch.Tensor, row_scale=None, col_scale=None, bias=None, a2=None, b2=None,
-                row_scale_inv: bool = False, out: torch.Tensor | None = None) -> torch.Tensor:
+                row_scale_inv: bool = False, out: torch.Tensor | None = None, err: torch.Tensor | None = None,
+                timeout_ns: int = 0) -> torch.Tensor:
     """``mh3_scaled_gemm``: bf16 (a b^T [+ a2 b2^T]) * rs[m] * cs[n] + bias[n].
 
     a [M,K], b [N,K]: both float8_e4m3fn or both bfloat16, last dim
     contiguous.  row_scale [M] / [M,1], col_scale [N] / [1,N] float32; bias
-    bf16 [N]; a2 [M,R], b2 [N,R] bf16 (optional low-rank term).
+    bf16 [N]; a2 [M,R], b2 [N,R] bf16 (optional low-rank term).  ``err``: an
+    int32 device word for wait timeouts (default: the library's own);
+    ``timeout_ns``: bound on every pipeline wait (0 = the library default).
     """
     lib = _lib.load()
     _require_cuda(a, b)
@@ -441,6 +449,11 @@ def scaled_gemm(a: torch.Tensor, b: torch.Tensor, row_scale=None, col_scale=None
         g.R = a2.shape[1]
         g.a2, g.lda2, g.b2, g.ldb2 = a2.data_ptr(), a2.stride(0), b2.data_ptr(), b2.stride(0)
     g.out, g.ldo = out.data_ptr(), out.stride(0)
+    if err is not None:
+        if err.dtype != torch.int32 or not err.is_cuda:
+            raise ValueError("err must be a CUDA int32 tensor")
+        g.err = err.data_ptr()
+    g.timeout_ns = int(timeout_ns)
     with torch.cuda.device(a.device):
         rc = lib.mh3_scaled_gemm(g, _stream(a.device))
     _lib.check(rc, "mh3_scaled_gemm")
@@ -478,8 +491,8 @@ def fp8_linear(x2d: torch.Tensor, w8: torch.Tensor, w_scale: torch.Tensor, bias,
     b2 = (scale*B)_cat / w_scale, both bf16, accumulated with the e4m3
     product before the row/column scales are applied.
     """
-    if x2d.dtype not in (torch.bfloat16, torch.float16):
-        x2d = x2d.to(torch.bfloat16)
+    if x2d.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        x2d = x2d.to(torch.float32)  # quantised from fp32 like the reference (fp8_linear.py:19)
     x2d = x2d.contiguous()
     M, K = x2d.shape
     N = w8.shape[0]

@@ -362,11 +362,13 @@ def compare(out: torch.Tensor, ref: torch.Tensor) -> dict:
     return {"cos": cos, "max_abs": err, "ref_absmax": scale, "max_abs_rel": err / max(scale, 1e-30)}
 
 
-def within_tolerance(r: dict, cos_min: float = 0.9995, max_abs: float = 2e-2) -> bool:
-    """The north-star tolerance: cos >= 0.9995 and max-abs <= 2e-2 * max(1, max|oracle|).
+def within_tolerance(r: dict, cos_min: float = 0.9995, max_abs_rel: float = 2e-2) -> bool:
+    """The north-star tolerance: cos >= 0.9995 and max-abs error <= 2e-2 x max|oracle|.
 
-    Absolute 2e-2 for outputs of unit scale or below; relative to the
-    oracle's largest magnitude above that (outlier channels push outputs
-    to ~10, where bf16 rounding of the output alone exceeds 2e-2).
+    The max-abs bound is read relative to the oracle's largest magnitude:
+    with the outlier-channel inputs outputs reach ~10, where the bf16
+    rounding of the output alone exceeds an absolute 2e-2; for outputs below
+    unit scale the relative reading is the stricter one.  ``compare``
+    reports the absolute error beside it (``max_abs``).
     """
-    return r["cos"] >= cos_min and r["max_abs"] <= max_abs * max(1.0, r["ref_absmax"])
+    return r["cos"] >= cos_min and r["max_abs"] <= max_abs_rel * r["ref_absmax"]

@@ -5,7 +5,7 @@ import os
 import pytest
 import torch
 
-from conftest import COS_MIN, GOLDEN
+from conftest import GOLDEN
 from oracle import fp8_attention_ref as OA
 
 pytestmark = pytest.mark.gpu
@@ -17,8 +17,17 @@ def _golden(name):
 
 
 @pytest.mark.parametrize("name", ["base_bn128", "mask_cross", "bias_cross", "d64_fp16", "repair_bn128"])
-def test_fp8_attention_on_reference_golden_inputs(name):
-    """Same inputs the reference's own kernels were run on (tests/golden)."""
+def test_fp8_attention_on_reference_golden_inputs(name, record_margin):
+    """Same inputs the reference's own kernels were run on (tests/golden).
+
+    The oracle is exact softmax attention on the operands the kernel really
+    multiplies: the reference's e4m3 Q and K bytes with their block scales
+    (this package's quantisation reproduces them bit for bit, see
+    test_quant_gpu) and, for the default f16 PV product, V as f16(v / scale_v)
+    times scale_v.  The north-star tolerance is asserted in its relative
+    reading (max-abs <= 2e-2 x max|oracle|), and the kernel must be at least
+    as accurate as the reference kernel's own output on the same inputs.
+    """
     from minimaxh3_b200.kernels.fp8_attention import fp8_attention
 
     g = _golden(name)
@@ -28,19 +37,18 @@ def test_fp8_attention_on_reference_golden_inputs(name):
     out = fp8_attention(q, k, v, scale=g["scale"], key_mask=km, key_bias=kb, repair_tau=g["repair_tau"])
     assert out.dtype == q.dtype and out.shape == q.shape
     out = out.float().cpu()
-    # The reference's quantised bytes (identical to ours, see test_quant_gpu)
-    # dequantised, then exact softmax attention.
-    B, H, Sq, D = g["q"].shape
     q8 = g["q8"].view(torch.float8_e4m3fn)
     k8 = g["k8"].view(torch.float8_e4m3fn)
-    v8 = g["v8t"].view(torch.float8_e4m3fn).transpose(2, 3)
+    sv = g["scale_v"].float()
+    v16 = (g["v"].float() / sv[:, :, None, :]).to(torch.float16)  # the f16 PV operand
     ref = OA.sdpa_dequant_oracle(OA.dequant_blocks(q8, g["scale_q"]), OA.dequant_blocks(k8, g["scale_k"]),
-                                 v8.double() * g["scale_v"].double()[:, :, None, :], 1.0,
+                                 v16.double() * sv.double()[:, :, None, :], 1.0,
                                  key_mask=g["key_mask"], key_bias=g["key_bias"], base2=True)
     r = OA.compare(out, ref)
-    r_ref = OA.compare(g["out"].float(), ref)  # the reference kernel's own error
-    assert r["cos"] >= COS_MIN, (r, r_ref)
-    assert r["cos"] >= r_ref["cos"], (r, r_ref)
+    r_ref = OA.compare(g["out"].float(), ref)  # the reference kernel's own error against the same oracle
+    record_margin(r)
+    assert OA.within_tolerance(r), (r, r_ref)
+    assert r["cos"] >= r_ref["cos"] and r["max_abs"] <= r_ref["max_abs"], (r, r_ref)
 
 
 def test_routed_sdpa_takes_fp8_branch():
