@@ -153,6 +153,106 @@ def _per_bh_e4m3(x):
     return x8, s[..., None].contiguous()
 
 
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def _reference_kernels():
+    """The reference's own ``kernels`` package (unmodified copy placed in baseline/_ref by
+    baseline/install_reference.py): its Triton FP8 attention and FP8 linear."""
+    if not os.path.isfile(os.path.join(REF_DIR, "kernels", "fp8_attention.py")):
+        raise FileNotFoundError("baseline/_ref has no reference copy (run baseline/install_reference.py)")
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    import importlib
+
+    return importlib.import_module("kernels.fp8_attention"), importlib.import_module("kernels.fp8_linear")
+
+
+def _median_ms(fn, stream, warmup=3, reps=20):
+    """BASELINE.md's competitor protocol: warm-ups, then the median of CUDA-event timings."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(reps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    return statistics.median(ts)
+
+
+def triton_competitor(q, k, v, stream):
+    """The reference's GPU path on the same box and inputs (BASELINE.md competitor 1).
+
+    (i) ``_fp8_attn_kernel`` alone - autotuned, warp-specialised on cc 10 - on
+    the operands its own wrapper makes (kernels/fp8_attention.py:300-402),
+    against this package's attention kernel on the drop-in path's operands
+    (per-128-row Q/K scales, f16 V/scale_v); (ii) ``fp8_attention(q, k, v)``
+    end to end on device-resident bf16 inputs, reference against this
+    package's drop-in.  3 warm-ups (the first call autotunes), median of 20.
+    """
+    import triton
+
+    from minimaxh3_b200 import ops
+    from minimaxh3_b200.kernels.fp8_attention import fp8_attention as mh3_fp8_attention
+
+    RF, _ = _reference_kernels()
+    Bq, Hq, Sq, Dq = q.shape
+    flop = 4.0 * Bq * Hq * Sq * k.shape[2] * Dq
+    res = {"source": "viragadel6/minimaxh3 kernels/fp8_attention.py, unmodified copy in baseline/_ref",
+           "protocol": "3 warm-ups (autotune on the first), median of 20 CUDA-event timings",
+           "inputs": "the headline workload's bf16 q, k, v on the device"}
+    res["triton_ref_e2e_ms"] = _median_ms(lambda: RF.fp8_attention(q, k, v), stream)
+    res["mh3_e2e_ms"] = _median_ms(lambda: mh3_fp8_attention(q, k, v), stream)
+    res["e2e_speedup"] = res["triton_ref_e2e_ms"] / res["mh3_e2e_ms"]
+    # (i) kernels alone: the reference wrapper's quantisation, then only its attention kernel
+    c = (1.0 / math.sqrt(Dq)) * RF.LOG2E
+    Sk = k.shape[2]
+    nq, nk = triton.cdiv(Sq, 128), triton.cdiv(Sk, 128)
+    dev = q.device
+    q8 = torch.empty((Bq, Hq, Sq, Dq), dtype=torch.float8_e4m3fn, device=dev)
+    sq = torch.empty((Bq, Hq, nq), dtype=torch.float32, device=dev)
+    RF._quantize_q_kernel[(nq, Bq * Hq)](q, q8, sq, Sq=Sq, H=Hq, D=Dq, stride_qb=q.stride(0),
+                                         stride_qh=q.stride(1), stride_qs=q.stride(2), stride_qd=q.stride(3),
+                                         c=float(c), BLOCK_M=128)
+    k_mean = k.float().mean(dim=2, keepdim=True).contiguous()
+    k8 = torch.empty((Bq, Hq, Sk, Dq), dtype=torch.float8_e4m3fn, device=dev)
+    sk = torch.empty((Bq, Hq, nk), dtype=torch.float32, device=dev)
+    RF._quantize_k_kernel[(nk, Bq * Hq)](k, k_mean, k8, sk, Sk=Sk, H=Hq, D=Dq, stride_kb=k.stride(0),
+                                         stride_kh=k.stride(1), stride_ks=k.stride(2), stride_kd=k.stride(3),
+                                         BLOCK_N=128)
+    del k_mean
+    v8t = torch.empty((Bq, Hq, Dq, Sk), dtype=torch.float8_e4m3fn, device=dev)
+    sv = torch.empty((Bq, Hq, Dq), dtype=torch.float32, device=dev)
+    RF._quantize_v_kernel[(Bq * Hq,)](v, v8t, sv, Sk=Sk, H=Hq, D=Dq, stride_vb=v.stride(0), stride_vh=v.stride(1),
+                                      stride_vs=v.stride(2), stride_vd=v.stride(3))
+    out = torch.empty_like(q)
+    is_cc10 = torch.cuda.get_device_capability(dev) >= (10, 0)
+
+    def ref_kernel():
+        RF._fp8_attn_kernel[(nq, Bq * Hq)](q8, k8, v8t, sq, sk, sv, q8, q8, out, Sq=Sq, Sk=Sk, H=Hq, D=Dq,
+                                           Sq_bucket=Sq // 512, Sk_bucket=Sk // 512, HAS_MASK=False,
+                                           HAS_BIAS=False, DO_REPAIR=False, repair_tau=-1.0, IS_CC10=is_cc10,
+                                           BLOCK_M=128)
+
+    res["triton_ref_kernel_ms"] = _median_ms(ref_kernel, stream)
+    best = getattr(RF._fp8_attn_kernel, "best_config", None)
+    res["triton_ref_best_config"] = str(best) if best is not None else None
+    del q8, k8, v8t, out
+    m8q, m8k, m8v, msq, msk, msv, _ = ops.quantize_qkv(q, k, v, c, v_dtype=torch.float16)
+    mout = torch.empty_like(q)
+    res["mh3_kernel_ms"] = _median_ms(
+        lambda: ops.attention_e4m3(m8q, m8k, m8v, msq, msk, msv, logit_scale_log2=1.0, out=mout), stream)
+    res["triton_ref_kernel_tflops"] = flop / res["triton_ref_kernel_ms"] / 1e9
+    res["mh3_kernel_tflops"] = flop / res["mh3_kernel_ms"] / 1e9
+    res["kernel_speedup"] = res["triton_ref_kernel_ms"] / res["mh3_kernel_ms"]
+    return res
+
+
 def cpu_reference_sample(seconds: float = 10.0):
     """The reference's CPU path (torch SDPA fallback) on a bounded sample of config 2."""
     from oracle.router_ref import cpu_sdpa_fallback
@@ -397,6 +497,13 @@ def run_gpu_arm(args, dist, rank, world, local):
             print(json.dumps({"value": value, "avg_launch_ms": avg_launch_ms, "achieved": achieved, "heads": H}))
         return
 
+    # The reference's own Triton path on the same box and inputs (after the timed region).
+    try:
+        competitor = triton_competitor(q, k, v, stream)
+    except Exception as e:  # noqa: BLE001 - reported in the line, not fatal
+        competitor = {"unavailable": f"{type(e).__name__}: {str(e)[:300]}"}
+    torch.cuda.empty_cache()
+
     # End to end through the drop-in API: pinned host bf16 in, bf16 out back to host.
     e2e_steps = max(1, min(args.steps, 3))
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
@@ -470,6 +577,21 @@ def run_gpu_arm(args, dist, rank, world, local):
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    line["competitor_same_box"] = competitor
+    # The rest of the metric on the same box (untimed by the driver's clock check: after the line's
+    # own timed regions): config 4 linear, config 3 varlen, ms per synthetic DiT block.
+    del hq, hk, hv, hout
+    torch.cuda.empty_cache()
+    extras = {}
+    for name, fn in (("config4_linear", lambda: linear_results(32760, 5, 3)),
+                     ("config3_varlen", lambda: varlen_results(5, 3)),
+                     ("dit_block", lambda: block_results(5, 3))):
+        try:
+            extras[name] = fn()
+        except Exception as e:  # noqa: BLE001
+            extras[name] = {"unavailable": f"{type(e).__name__}: {str(e)[:300]}"}
+        torch.cuda.empty_cache()
+    line["extras"] = extras
     print(json.dumps(line), flush=True)
 
 
@@ -488,6 +610,10 @@ def _time_cuda(fn, steps, warmup, stream):
 
 
 def run_linear_workload(args):
+    print(json.dumps(linear_results(args.linear_rows, args.steps, args.warmup)), flush=True)
+
+
+def linear_results(M, steps, warmup):
     """FP8 scaled linear with fused epilogue (not the headline).
 
     M=32760 tokens, K=5120, N in {5120, 15360, 13824}; x N(0,1) bf16, W N(0,0.02),
@@ -506,10 +632,13 @@ def run_linear_workload(args):
     dev = torch.device("cuda", 0)
     stream = torch.cuda.current_stream(dev)
     g = torch.Generator(device=dev).manual_seed(0)
-    M = args.linear_rows
     xs = {}
     lines = []
     peaks = _peaks()
+    try:
+        _, RL = _reference_kernels()
+    except Exception as e:  # noqa: BLE001 - reported, not fatal
+        RL, ref_missing = None, f"{type(e).__name__}: {e}"
     for N, K in ((5120, 5120), (15360, 5120), (13824, 5120), (5120, 13824)):  # last: MLP-down
         x = xs.setdefault(K, torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16))
         lin = torch.nn.Linear(K, N, device=dev, dtype=torch.bfloat16)
@@ -524,27 +653,38 @@ def run_linear_workload(args):
         sb = mod.w_scale.reshape(-1)
         flop = 2.0 * M * N * K
         t_gemm = _time_cuda(lambda: ops.scaled_gemm(x8, mod.w8, row_scale=sa, col_scale=sb, bias=mod.bias),
-                            args.steps, args.warmup, stream)
-        t_fwd = _time_cuda(lambda: mod(x), args.steps, args.warmup, stream)
+                            steps, warmup, stream)
+        t_fwd = _time_cuda(lambda: mod(x), steps, warmup, stream)
+        t_refmod = None
+        if RL is not None:
+            # the reference's own FP8Linear (Triton row quantisation + torch._scaled_mm + LoRA matmuls)
+            rlin = torch.nn.Linear(K, N, device=dev, dtype=torch.bfloat16)
+            with torch.no_grad():
+                rlin.weight.copy_(torch.randn(N, K, generator=g, device=dev) * 0.02)
+                rlin.bias.copy_(mod.bias)
+            rmod = RL.FP8Linear.from_linear(rlin)
+            rmod.adapters = [(A, Bm, 1.0)]
+            t_refmod = _median_ms(lambda: rmod(x), stream)
+            del rmod, rlin
 
         def ref_recipe():
             out = torch._scaled_mm(x8, mod.w8.t(), scale_a=sa, scale_b=mod.w_scale, bias=mod.bias,
                                    out_dtype=torch.bfloat16)
             return out + ((x @ A.t()) @ Bm.t()).to(out.dtype)
 
-        t_ref = _time_cuda(ref_recipe, args.steps, args.warmup, stream)
+        t_ref = _time_cuda(ref_recipe, steps, warmup, stream)
         t_cub = _time_cuda(lambda: torch._scaled_mm(x8, mod.w8.t(), scale_a=sa, scale_b=mod.w_scale, bias=mod.bias,
-                                                    out_dtype=torch.bfloat16), args.steps, args.warmup, stream)
+                                                    out_dtype=torch.bfloat16), steps, warmup, stream)
         # unquantised nn.Linear + the same adapter (runtime/lora.py:206-226): one fused bf16
         # GEMM against the reference's cuBLAS linear + two LoRA matmuls + add
         w16 = (torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
-        t_l16 = _time_cuda(lambda: ops.linear_lora(x, w16, mod.bias, [(A, Bm, 1.0)]), args.steps, args.warmup, stream)
+        t_l16 = _time_cuda(lambda: ops.linear_lora(x, w16, mod.bias, [(A, Bm, 1.0)]), steps, warmup, stream)
 
         def ref_bf16():
             out = torch.nn.functional.linear(x, w16, mod.bias)
             return out + ((x @ A.t()) @ Bm.t()).to(out.dtype)
 
-        t_r16 = _time_cuda(ref_bf16, args.steps, args.warmup, stream)
+        t_r16 = _time_cuda(ref_bf16, steps, warmup, stream)
         del w16
         lines.append({"N": N, "K": K, "gemm_ms": t_gemm, "gemm_tflops": flop / t_gemm / 1e9,
                       "cublas_scaled_mm_tflops": flop / t_cub / 1e9,
@@ -552,13 +692,22 @@ def run_linear_workload(args):
                       "fp8linear_forward_ms": t_fwd, "fp8linear_forward_tflops": flop / t_fwd / 1e9,
                       "reference_recipe_ms": t_ref, "reference_recipe_tflops": flop / t_ref / 1e9,
                       "bf16_linear_lora_tflops": flop / t_l16 / 1e9,
-                      "bf16_reference_recipe_tflops": flop / t_r16 / 1e9})
-    print(json.dumps({"workload": f"config4: FP8 scaled linear M={M} K=5120 (N 5120/15360/13824) and the MLP-down "
-                                  "shape K=13824 N=5120, LoRA r=32", "unit": "TFLOP/s",
-                      "peak": peaks, "results": lines}), flush=True)
+                      "bf16_reference_recipe_tflops": flop / t_r16 / 1e9,
+                      "reference_fp8linear_forward_ms": t_refmod,
+                      "reference_fp8linear_forward_tflops": flop / t_refmod / 1e9 if t_refmod else None,
+                      "forward_speedup_vs_reference_module": t_refmod / t_fwd if t_refmod else None})
+        del mod, lin, x8, sa
+    return {"workload": f"config4: FP8 scaled linear M={M} K=5120 (N 5120/15360/13824) and the MLP-down "
+                        "shape K=13824 N=5120, LoRA r=32", "unit": "TFLOP/s", "peak": peaks,
+            "reference_module": "baseline/_ref kernels/fp8_linear.py FP8Linear (median of 20 after 3 warm-ups)"
+            if RL is not None else f"unavailable: {ref_missing}", "results": lines}
 
 
 def run_varlen_workload(args):
+    print(json.dumps(varlen_results(args.steps, args.warmup)), flush=True)
+
+
+def varlen_results(steps, warmup):
     """packed varlen, cu_seqlens [0, 33784, 50676], H=40 D=128.
 
     e4m3 q/k/v with per-(sequence, head) scales (synthetic N(0,1) with one
@@ -592,15 +741,19 @@ def run_varlen_workload(args):
     out = torch.empty(T, Hh, Dd, dtype=torch.bfloat16, device=dev)
     call = lambda: ops.attention_e4m3(q8, k8, v16, *scales, logit_scale_log2=ls2, cu_seqlens_q=cu,
                                       cu_seqlens_k=cu, max_seqlen_q=max(lens), out=out)
-    ms = _time_cuda(call, args.steps, args.warmup, stream)
+    ms = _time_cuda(call, steps, warmup, stream)
     flop = 4.0 * Hh * Dd * sum(L * L for L in lens)
     peaks = _peaks()
-    print(json.dumps({"workload": "config3: varlen cu_seqlens [0,33784,50676], H=40 D=128, per-(seq,head) "
-                                  "scales, f16 PV", "unit": "TFLOP/s", "ms": ms, "tflops": flop / ms / 1e9,
-                      "frac_of_fp8_peak": flop / ms / 1e9 / peaks["fp8_tflops"], "flop": flop}), flush=True)
+    return {"workload": "config3: varlen cu_seqlens [0,33784,50676], H=40 D=128, per-(seq,head) "
+                        "scales, f16 PV", "unit": "TFLOP/s", "ms": ms, "tflops": flop / ms / 1e9,
+            "frac_of_fp8_peak": flop / ms / 1e9 / peaks["fp8_tflops"], "flop": flop}
 
 
 def run_block_workload(args):
+    print(json.dumps(block_results(args.steps, args.warmup)), flush=True)
+
+
+def block_results(steps, warmup):
     """ms per synthetic DiT block at config 2 / 4 shapes (the full transformer
     and its block count are not available): QKV projection FP8Linear
     (5120 -> 15360), self-attention through the drop-in fp8_attention on
@@ -638,12 +791,12 @@ def run_block_workload(args):
         c = fp8_attention(h.view(1, M, Hh, Dd).transpose(1, 2), tk, tv).transpose(1, 2).reshape(M, C)
         return mlp_up(c)
 
-    ms = _time_cuda(block, args.steps, args.warmup, stream)
+    ms = _time_cuda(block, steps, warmup, stream)
     flop = (2.0 * M * C * (3 * C + C + 13824) + 4.0 * Hh * M * M * Dd + 4.0 * Hh * M * T * Dd)
-    print(json.dumps({"workload": "synthetic DiT block: QKV GEMM N=15360 + self-attention S=32760 + out-proj "
-                                  "N=5120 + cross-attention to 512 tokens + MLP-up N=13824 (LoRA r=32 on each "
-                                  "linear); per DiT step = this x num_blocks (num_blocks not available)",
-                      "unit": "ms", "ms_per_block": ms, "tflops": flop / ms / 1e9}), flush=True)
+    return {"workload": "synthetic DiT block: QKV GEMM N=15360 + self-attention S=32760 + out-proj "
+                        "N=5120 + cross-attention to 512 tokens + MLP-up N=13824 (LoRA r=32 on each "
+                        "linear); per DiT step = this x num_blocks (num_blocks not available)",
+            "unit": "ms", "ms_per_block": ms, "tflops": flop / ms / 1e9}
 
 
 def run_quant_workload(args):

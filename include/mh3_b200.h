@@ -35,7 +35,8 @@ extern "C" {
 /* ABI history: 1: the first release, mh3_quantize_qkv_noalloc included;
  * 2: mh3_attn_args.kv_len; 3: head selection in mh3_absmax_bh /
  * mh3_quantize_bh, mh3_copy_rows, mh3_step_diff; 4: f32 input to
- * mh3_quantize_rows. */
+ * mh3_quantize_rows, test_flags in mh3_attn_args (was reserved0) and
+ * mh3_gemm_args. */
 #define MH3_ABI_VERSION 4
 
 #define MH3_OK 0
@@ -52,6 +53,14 @@ extern "C" {
 /* Device-side error codes written by kernels into an ``err`` word. */
 #define MH3_DEVERR_NONE 0
 #define MH3_DEVERR_WAIT_TIMEOUT 1 /* an mbarrier wait exceeded timeout_ns */
+
+/* test_flags bits (attention and GEMM arguments).  MH3_TEST_STALL_PRODUCER:
+ * each CTA's load warp first waits on a barrier nothing arrives on, so its
+ * bounded wait runs out after timeout_ns; the kernel then records
+ * MH3_DEVERR_WAIT_TIMEOUT, issues no copy, runs its other waits to their
+ * abort path, frees its tensor memory and returns (the output is
+ * unspecified).  For testing the failure path without a GPU fault. */
+#define MH3_TEST_STALL_PRODUCER 1
 
 MH3_API int mh3_abi_version(void);
 
@@ -96,7 +105,7 @@ typedef struct mh3_attn_args {
   int32_t batch, heads, seqlen_q, seqlen_k, head_dim; /* head_dim: 64 or 128 */
   int32_t out_dtype;                                   /* MH3_DTYPE_BF16 / MH3_DTYPE_F16 */
   int32_t v_dtype;                                     /* MH3_DTYPE_E4M3 / MH3_DTYPE_F16 */
-  int32_t reserved0;
+  int32_t test_flags;                                  /* 0; MH3_TEST_* bits for tests of the bounded waits */
   const void* q8;
   int64_t q_stride_b, q_stride_h, q_stride_s; /* multiples of 16 (v: of 16 bytes) */
   const void* k8;
@@ -238,6 +247,8 @@ typedef struct mh3_gemm_args {
   int64_t ldo;
   int* err;
   uint64_t timeout_ns;
+  int32_t test_flags; /* 0; MH3_TEST_* bits (ABI version 4) */
+  int32_t reserved1;
 } mh3_gemm_args;
 
 MH3_API int mh3_scaled_gemm(const mh3_gemm_args* args, void* stream);

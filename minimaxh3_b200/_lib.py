@@ -23,6 +23,7 @@ MH3_DTYPE_F16 = 1
 MH3_DTYPE_E4M3 = 2
 MH3_DTYPE_F32 = 3
 MH3_DEVERR_WAIT_TIMEOUT = 1
+MH3_TEST_STALL_PRODUCER = 1
 
 c_i32 = ctypes.c_int32
 c_i64 = ctypes.c_int64
@@ -36,7 +37,7 @@ class AttnArgs(ctypes.Structure):
 
     _fields_ = [
         ("batch", c_i32), ("heads", c_i32), ("seqlen_q", c_i32), ("seqlen_k", c_i32),
-        ("head_dim", c_i32), ("out_dtype", c_i32), ("v_dtype", c_i32), ("reserved0", c_i32),
+        ("head_dim", c_i32), ("out_dtype", c_i32), ("v_dtype", c_i32), ("test_flags", c_i32),
         ("q8", c_ptr), ("q_stride_b", c_i64), ("q_stride_h", c_i64), ("q_stride_s", c_i64),
         ("k8", c_ptr), ("k_stride_b", c_i64), ("k_stride_h", c_i64), ("k_stride_s", c_i64),
         ("v8", c_ptr), ("v_stride_b", c_i64), ("v_stride_h", c_i64), ("v_stride_s", c_i64),
@@ -78,6 +79,7 @@ class GemmArgs(ctypes.Structure):
         ("row_scale", c_ptr), ("col_scale", c_ptr), ("bias", c_ptr),
         ("a2", c_ptr), ("lda2", c_i64), ("b2", c_ptr), ("ldb2", c_i64),
         ("out", c_ptr), ("ldo", c_i64), ("err", c_ptr), ("timeout_ns", c_u64),
+        ("test_flags", c_i32), ("reserved1", c_i32),
     ]
 
 

@@ -89,6 +89,7 @@ struct Params {
   int* err;
   unsigned long long timeout_ns;
   const int* kv_len;  // per-batch key count (padding past it is skipped), or null
+  int test_flags;     // MH3_TEST_* bits (tests of the bounded waits); 0 in normal use
 };
 
 template <int D, bool PV16>
@@ -105,6 +106,7 @@ struct __align__(1024) Smem {
   uint64_t bar_sld[2];  // softmax has read S(j) into registers
   uint64_t bar_p[2][4];  // [tile][key part]: that part of P(j) is in TMEM
   uint64_t bar_o;
+  uint64_t bar_never;  // nothing arrives on it (test hook)
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -164,6 +166,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
       for (int k = 0; k < 4; ++k) mbar_init(smem_u32(&sm.bar_p[i][k]), 4);
     }
     mbar_init(smem_u32(&sm.bar_o), 1);
+    mbar_init(smem_u32(&sm.bar_never), 1);
     sm.abort_flag = 0;
     fence_mbar_init();
   }
@@ -178,18 +181,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
   const WaitGuard g{&sm.abort_flag, p.err, p.timeout_ns};
 
   if (warp >= 8) {
-    setmaxnreg_dec<64>();
+    setmaxnreg_dec<80>();
     if (warp == 8 && lane == 0) {
       // ---------------------------------------------------------------- producer
       tma_prefetch_desc(&p.tmq);
       tma_prefetch_desc(&p.tmk);
       tma_prefetch_desc(&p.tmv);
+      // Test hook (MH3_TEST_STALL_PRODUCER): wait on a barrier nothing arrives
+      // on, so the bounded wait runs out and the CTA takes its abort path
+      // with no copy issued.
+      const bool go = (p.test_flags & MH3_TEST_STALL_PRODUCER) == 0 || mbar_wait(smem_u32(&sm.bar_never), 0, g);
       const uint32_t bq = smem_u32(&sm.bar_q);
-      mbar_arrive_expect_tx(bq, 2 * BM * D);
-      tma_load_4d(smem_u32(sm.q[0]), &p.tmq, bq, 0, q_start + qt0 * BM, h, bcoord);
-      tma_load_4d(smem_u32(sm.q[1]), &p.tmq, bq, 0, q_start + (qt0 + 1) * BM, h, bcoord);
+      if (go) {
+        mbar_arrive_expect_tx(bq, 2 * BM * D);
+        tma_load_4d(smem_u32(sm.q[0]), &p.tmq, bq, 0, q_start + qt0 * BM, h, bcoord);
+        tma_load_4d(smem_u32(sm.q[1]), &p.tmq, bq, 0, q_start + (qt0 + 1) * BM, h, bcoord);
+      }
       int issued = 0;
-      for (int j = 0; j < nk; ++j) {
+      for (int j = 0; go && j < nk; ++j) {
         const int ks = j % KST;
         const uint32_t kph = (uint32_t)(j / KST) & 1u;
         if (!mbar_wait(smem_u32(&sm.bar_kempty[ks]), kph ^ 1u, g)) break;
@@ -216,7 +225,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
       // Teardown: let the last copy issued into each stage land before exit.
       const int nk_issued = issued >= 0 ? issued : -issued;
       const int nv_issued = issued >= 0 ? issued : -issued - 1;
-      mbar_wait_teardown(bq, 0);
+      if (go) mbar_wait_teardown(bq, 0);
       for (int j = (nk_issued > KST ? nk_issued - KST : 0); j < nk_issued; ++j)
         mbar_wait_teardown(smem_u32(&sm.bar_kfull[j % KST]), (uint32_t)(j / KST) & 1u);
       for (int j = (nv_issued > VST ? nv_issued - VST : 0); j < nv_issued; ++j)
@@ -234,31 +243,37 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
       constexpr bool kEarlyHalf = MH3_EARLY_HALF;
       constexpr int kPHalves = PParts<PV16>::N;
       constexpr uint32_t kIdescO = PV16 ? idesc_f16(BM, D, false, true) : idesc_e4m3(BM, D, false, true);
-      const uint32_t tS[2] = {tmem + 0u, tmem + 128u};
-      const uint32_t tO[2] = {tmem + 256u, tmem + 256u + (uint32_t)D};
-      const uint32_t q_base[2] = {smem_u32(sm.q[0]), smem_u32(sm.q[1])};
-      // K-major operands (Q, K): 8-row swizzle atoms of D bytes per row, K
-      // advanced 32 bytes (32 e4m3) per MMA.  MN-major V: one swizzle atom
-      // across D channels, 8-key groups D*8 bytes apart, 32 keys per MMA.
-      auto kmaj = [&](uint32_t base, int kk) { return smem_desc(base + kk * 32, 16, 8 * kRowBytes, kLayout); };
-      auto vdesc = [&](int vs, int kk) {
-        if constexpr (PV16)  // 16 keys per MMA; atom columns of 64 channels, BN*128 bytes apart
-          return smem_desc(smem_u32(sm.v[vs]) + kk * 16 * 128, BN * 128, 8 * 128, kLayoutSW128);
-        else
-          return smem_desc(smem_u32(sm.v[vs]) + kk * 32 * kRowBytes, kTileBytes, 8 * kRowBytes, kLayout);
-      };
+      // Descriptors are built once: a Q tile, K/V stage or K step only moves
+      // the start-address field (bytes >> 4).  K-major operands (Q, K): 8-row
+      // swizzle atoms of D bytes per row, 32 bytes (32 e4m3) of K per MMA.
+      // MN-major V: e4m3 - one swizzle atom across D channels, 32 keys per
+      // MMA; f16 - 64-channel atom columns BN*128 bytes apart, 16 keys per MMA.
+      const uint64_t dq0 = smem_desc(smem_u32(sm.q[0]), 16, 8 * kRowBytes, kLayout);
+      const uint64_t dk0 = smem_desc(smem_u32(sm.k[0]), 16, 8 * kRowBytes, kLayout);
+      const uint64_t dv0 = PV16 ? smem_desc(smem_u32(sm.v[0]), BN * 128, 8 * 128, kLayoutSW128)
+                                : smem_desc(smem_u32(sm.v[0]), kTileBytes, 8 * kRowBytes, kLayout);
+      constexpr uint64_t kQStep = (BM * D) >> 4;
+      constexpr uint64_t kKStage = kTileBytes >> 4;
+      constexpr uint64_t kVStage = kVTileBytes >> 4;
+      constexpr uint64_t kVk = PV16 ? (16 * 128) >> 4 : (32 * kRowBytes) >> 4;
+      auto tS = [&](int t) { return tmem + (uint32_t)(t * 128); };
+      auto tO = [&](int t) { return tmem + 256u + (uint32_t)(t * D); };
       auto issue_s = [&](int t, int ks) {
-        const uint32_t kb = smem_u32(sm.k[ks]);
+        const uint64_t dq = dq0 + (uint64_t)t * kQStep;
+        const uint64_t dk = dk0 + (uint64_t)ks * kKStage;
+        mma_f8_ss(tS(t), dq, dk, kIdescS, 0u);
 #pragma unroll
-        for (int kk = 0; kk < D / 32; ++kk) mma_f8_ss(tS[t], kmaj(q_base[t], kk), kmaj(kb, kk), kIdescS, kk > 0);
+        for (int kk = 1; kk < D / 32; ++kk) mma_f8_ss(tS(t), dq + 2u * kk, dk + 2u * kk, kIdescS, 1u);
       };
       // Half of S(t, j+1): keys [half*64, half*64+64) into S columns
       // [half*64, half*64+64) (N = 64; K rows 64.. start on a swizzle atom).
       auto issue_s_half = [&](int t, int ks, int half) {
-        const uint32_t kb = smem_u32(sm.k[ks]) + (uint32_t)(half * (BN / 2) * kRowBytes);
+        const uint64_t dq = dq0 + (uint64_t)t * kQStep;
+        const uint64_t dk = dk0 + (uint64_t)ks * kKStage + (uint64_t)((half * (BN / 2) * kRowBytes) >> 4);
+        const uint32_t d = tS(t) + (uint32_t)(half * (BN / 2));
+        mma_f8_ss(d, dq, dk, kIdescS64, 0u);
 #pragma unroll
-        for (int kk = 0; kk < D / 32; ++kk)
-          mma_f8_ss(tS[t] + (uint32_t)(half * (BN / 2)), kmaj(q_base[t], kk), kmaj(kb, kk), kIdescS64, kk > 0);
+        for (int kk = 1; kk < D / 32; ++kk) mma_f8_ss(d, dq + 2u * kk, dk + 2u * kk, kIdescS64, 1u);
       };
       bool ok = mbar_wait(smem_u32(&sm.bar_q), 0, g);
       if (nk > 0) {
@@ -293,14 +308,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
             mbar_wait(smem_u32(&sm.bar_p[t][hf]), (uint32_t)j & 1u, g);
             tc_fence_after();
             constexpr int kPer = (PV16 ? BN / 16 : BN / 32) / kPHalves;
-            if constexpr (PV16) {
+            const uint64_t dv = dv0 + (uint64_t)vs * kVStage;
 #pragma unroll
-              for (int kk = hf * kPer; kk < hf * kPer + kPer; ++kk)
-                mma_f16_ts(tO[t], tS[t] + (uint32_t)(kk * 8), vdesc(vs, kk), kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
-            } else {
-#pragma unroll
-              for (int kk = hf * kPer; kk < hf * kPer + kPer; ++kk)
-                mma_f8_ts(tO[t], tS[t] + (uint32_t)(kk * 8), vdesc(vs, kk), kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = hf * kPer; kk < hf * kPer + kPer; ++kk) {
+              const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
+              if constexpr (PV16)
+                mma_f16_ts(tO(t), tS(t) + (uint32_t)(kk * 8), dv + kVk * kk, kIdescO, acc);
+              else
+                mma_f8_ts(tO(t), tS(t) + (uint32_t)(kk * 8), dv + kVk * kk, kIdescO, acc);
             }
           }
           if (t == 1) mma_commit(smem_u32(&sm.bar_vempty[vs]));
@@ -321,7 +336,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
     }
   } else {
     // ------------------------------------------------------------------ softmax
-    setmaxnreg_inc<216>();
+    setmaxnreg_inc<200>();
     const int t = warp >> 2;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
@@ -337,7 +352,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
 
     float m = -1.0e30f;  // running max (log2 units), raised lazily; -1e30 = no key yet
     float l = 0.0f;  // running sum of P
+    // K scale of the current tile, loaded one tile ahead so that its latency
+    // overlaps the wait for S (block scales change every tile).
+    float sk_cur = nk > 0 ? __ldg(skp) : 1.0f;
     for (int j = 0; j < nk; ++j) {
+      const float sk_next = (j + 1 < nk) ? __ldg(skp + (long long)(j + 1) * p.skblk) : 1.0f;
       mbar_wait(smem_u32(&sm.bar_s[t]), (uint32_t)j & 1u, g);
       tc_fence_after();
       uint32_t sr[4][32];
@@ -349,7 +368,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) fwd_kernel(const __grid_consta
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&sm.bar_sld[t]));
 
-      const float c_tile = cq * __ldg(skp + (long long)j * p.skblk);
+      const float c_tile = cq * sk_cur;
+      sk_cur = sk_next;
       const int rem = k_len - j * BN;
       // Raw S chunk c (32 keys) -> the value P is taken from: s*c + bias2 with
       // bias2 = -inf for masked or padding keys (HAS_BIAS), else s with the
@@ -623,6 +643,7 @@ extern "C" int mh3_fp8_attention_fwd(const mh3_attn_args* a, void* stream) {
   p.err = a->err ? a->err : device_error_word();
   p.timeout_ns = a->timeout_ns ? a->timeout_ns : 4000000000ull;
   p.kv_len = a->kv_len;
+  p.test_flags = a->test_flags;
 
   const int max_q = varlen ? a->max_seqlen_q : a->seqlen_q;
   const int q_tiles = (max_q + attn::BM - 1) / attn::BM;

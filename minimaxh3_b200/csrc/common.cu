@@ -50,19 +50,41 @@ int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, voi
   return MH3_OK;
 }
 
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+void* current_context() {
+  static std::once_flag once;
+  static CtxGetCurrentFn fn = nullptr;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(ptr);
+  });
+  CUcontext ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+  return ctx;
+}
+
 // One error word per device, in the module's global memory.
 __device__ int g_device_error;
 
 int* device_error_word() {
   constexpr int kMaxDevices = 64;
   static int* addr[kMaxDevices] = {};
+  static void* ctx_of[kMaxDevices] = {};
   static std::mutex mu;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
   std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
+  // Looked up again when the device's context changed (e.g. after a device
+  // reset): the module, and with it the word, is loaded anew there.
+  void* ctx = current_context();
+  if (addr[dev] == nullptr || ctx_of[dev] != ctx) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_device_error) == cudaSuccess) addr[dev] = static_cast<int*>(p);
+    addr[dev] = cudaGetSymbolAddress(&p, g_device_error) == cudaSuccess ? static_cast<int*>(p) : nullptr;
+    ctx_of[dev] = ctx;
   }
   return addr[dev];
 }

@@ -53,6 +53,7 @@ struct Params {
   long long ldo;
   int* err;
   unsigned long long timeout_ns;
+  int test_flags;  // MH3_TEST_* bits (tests of the bounded waits); 0 in normal use
 };
 
 template <int BN>
@@ -64,6 +65,7 @@ struct __align__(1024) Smem {
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint64_t mma_done;
+  uint64_t bar_never;  // nothing arrives on it (test hook)
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -110,6 +112,7 @@ __global__ void __launch_bounds__(NUM_THREADS, BN == 64 ? 2 : 1) gemm_kernel(con
       mbar_init(smem_u32(&sm.acc_empty[i]), 4);
     }
     mbar_init(smem_u32(&sm.mma_done), 1);
+    mbar_init(smem_u32(&sm.bar_never), 1);
     sm.abort_flag = 0;
     fence_mbar_init();
   }
@@ -135,7 +138,8 @@ __global__ void __launch_bounds__(NUM_THREADS, BN == 64 ? 2 : 1) gemm_kernel(con
       }
       int it = 0;
       int last_issued = -1;
-      bool ok = true;
+      // Test hook (MH3_TEST_STALL_PRODUCER): a wait nothing ends runs out first.
+      bool ok = (p.test_flags & MH3_TEST_STALL_PRODUCER) == 0 || mbar_wait(smem_u32(&sm.bar_never), 0, g);
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int mb, nb;
         coords(t, mb, nb);
@@ -319,6 +323,7 @@ struct __align__(1024) SmemPair {
   uint64_t acc_full[2];
   uint64_t acc_empty[2];       // used in the leader: 4 warps x 2 CTAs
   uint64_t mma_done;
+  uint64_t bar_never;  // nothing arrives on it (test hook)
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -366,6 +371,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_pair_kernel(const __grid_
       mbar_init(smem_u32(&sm.acc_empty[i]), 8);
     }
     mbar_init(smem_u32(&sm.mma_done), 1);
+    mbar_init(smem_u32(&sm.bar_never), 1);
     sm.abort_flag = 0;
     fence_mbar_init();
   }
@@ -394,7 +400,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_pair_kernel(const __grid_
     __syncwarp();
     int it = 0;
     int last_issued = -1;
+    // Test hook (MH3_TEST_STALL_PRODUCER): a wait nothing ends runs out first
+    // (one lane waits, the warp takes its answer).
     bool ok = true;
+    if (p.test_flags & MH3_TEST_STALL_PRODUCER) {
+      bool w = true;
+      if (lane == 0) w = mbar_wait(smem_u32(&sm.bar_never), 0, g);
+      ok = __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
+    }
     for (int t = pair; t < num_tiles && ok; t += npairs) {
       int mb, nb;
       coords(t, mb, nb);
@@ -696,6 +709,7 @@ extern "C" int mh3_scaled_gemm(const mh3_gemm_args* a, void* stream) {
   p.ldo = a->ldo;
   p.err = a->err ? a->err : device_error_word();
   p.timeout_ns = a->timeout_ns ? a->timeout_ns : 4000000000ull;
+  p.test_flags = a->test_flags;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const cudaError_t e = use_pair ? gemm::launch_pair(p, st) : BN == 64 ? gemm::launch<64>(p, st) : gemm::launch<256>(p, st);
   if (e != cudaSuccess) return fail_cuda(e, "mh3_scaled_gemm launch");

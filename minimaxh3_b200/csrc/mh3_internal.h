@@ -28,4 +28,8 @@ int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, voi
 // The library's device error word on the current device.
 int* device_error_word();
 
+// The calling thread's current CUDA context (CUcontext), or null; through
+// the runtime's driver entry point, so the library does not link libcuda.
+void* current_context();
+
 }  // namespace mh3

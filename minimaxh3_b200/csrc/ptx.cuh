@@ -79,18 +79,19 @@ struct WaitGuard {
 // up after ``g.timeout_ns`` of wall time (or at once if another thread has
 // already given up): records kErrWaitTimeout in the error word, raises the
 // CTA abort flag and returns false.  Never traps.
+// The time limit is checked after every failed try (a try_wait may itself
+// suspend the thread for a short while), so a limit of a few microseconds
+// is observed even by waits that last only a few tries.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitGuard& g) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 1;; ++it) {
+  for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 15u) == 0u) {
-      if (*g.abort_flag) return false;
-      if (globaltimer_ns() - t0 > g.timeout_ns) {
-        *g.abort_flag = 1;
-        if (g.err) atomicCAS(g.err, 0, (int)kErrWaitTimeout);
-        return false;
-      }
+    if (*g.abort_flag) return false;
+    if (globaltimer_ns() - t0 > g.timeout_ns) {
+      *g.abort_flag = 1;
+      if (g.err) atomicCAS(g.err, 0, (int)kErrWaitTimeout);
+      return false;
     }
   }
 }
@@ -112,15 +113,13 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
 __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, const WaitGuard& g) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 1;; ++it) {
+  for (;;) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((it & 15u) == 0u) {
-      if (*g.abort_flag) return false;
-      if (globaltimer_ns() - t0 > g.timeout_ns) {
-        *g.abort_flag = 1;
-        if (g.err) atomicCAS(g.err, 0, (int)kErrWaitTimeout);
-        return false;
-      }
+    if (*g.abort_flag) return false;
+    if (globaltimer_ns() - t0 > g.timeout_ns) {
+      *g.abort_flag = 1;
+      if (g.err) atomicCAS(g.err, 0, (int)kErrWaitTimeout);
+      return false;
     }
   }
 }

@@ -656,21 +656,26 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 // Device address of g_noalloc_scratch on the current device.  In host code
 // the symbol names a host-side stand-in, not device memory, so the address
-// is looked up once per device (with that device current) and cached.
+// is looked up once per device (with that device current) and cached; it is
+// looked up again if the device's context changed since (a device reset
+// loads the module, and the array, anew).
 static int noalloc_scratch(void** out) {
   constexpr int kMaxDevices = 64;
   static void* addr[kMaxDevices] = {};
+  static void* ctx_of[kMaxDevices] = {};
   static std::mutex mu;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail_cuda(e, "mh3_quantize_qkv_noalloc: cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return fail(MH3_ERR_UNSUPPORTED, "device index out of range");
   std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
+  void* ctx = current_context();
+  if (addr[dev] == nullptr || ctx_of[dev] != ctx) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return fail_cuda(e, "mh3_quantize_qkv_noalloc: cudaGetSymbolAddress");
     addr[dev] = p;
+    ctx_of[dev] = ctx;
   }
   *out = addr[dev];
   return MH3_OK;

@@ -107,6 +107,7 @@ def attention_e4m3(
     err: torch.Tensor | None = None,
     timeout_ns: int = 0,
     kv_len: torch.Tensor | None = None,
+    test_flags: int = 0,
 ) -> torch.Tensor:
     """Non-causal FP8 attention (``mh3_fp8_attention_fwd``).
 
@@ -195,6 +196,7 @@ def attention_e4m3(
     if err is not None:
         a.err = err.data_ptr()
     a.timeout_ns = int(timeout_ns)
+    a.test_flags = int(test_flags)
     if kv_len is not None:
         if kv_len.dtype != torch.int32 or kv_len.numel() < a.batch or not kv_len.is_cuda:
             raise ValueError("kv_len must be a CUDA int32 tensor with one entry per batch")
@@ -400,14 +402,15 @@ def quantize_bh(x: torch.Tensor, scale: torch.Tensor, out_dtype: torch.dtype = E
 
 def scaled_gemm(a: torch.Tensor, b: torch.Tensor, row_scale=None, col_scale=None, bias=None, a2=None, b2=None,
                 row_scale_inv: bool = False, out: torch.Tensor | None = None, err: torch.Tensor | None = None,
-                timeout_ns: int = 0) -> torch.Tensor:
+                timeout_ns: int = 0, test_flags: int = 0) -> torch.Tensor:
     """``mh3_scaled_gemm``: bf16 (a b^T [+ a2 b2^T]) * rs[m] * cs[n] + bias[n].
 
     a [M,K], b [N,K]: both float8_e4m3fn or both bfloat16, last dim
     contiguous.  row_scale [M] / [M,1], col_scale [N] / [1,N] float32; bias
     bf16 [N]; a2 [M,R], b2 [N,R] bf16 (optional low-rank term).  ``err``: an
     int32 device word for wait timeouts (default: the library's own);
-    ``timeout_ns``: bound on every pipeline wait (0 = the library default).
+    ``timeout_ns``: bound on every pipeline wait (0 = the library default);
+    ``test_flags``: MH3_TEST_* bits (tests of the bounded waits only).
     """
     lib = _lib.load()
     _require_cuda(a, b)
@@ -454,6 +457,7 @@ def scaled_gemm(a: torch.Tensor, b: torch.Tensor, row_scale=None, col_scale=None
             raise ValueError("err must be a CUDA int32 tensor")
         g.err = err.data_ptr()
     g.timeout_ns = int(timeout_ns)
+    g.test_flags = int(test_flags)
     with torch.cuda.device(a.device):
         rc = lib.mh3_scaled_gemm(g, _stream(a.device))
     _lib.check(rc, "mh3_scaled_gemm")

@@ -397,7 +397,7 @@ def make_cpu_fallback(A, out_dir):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="checkout of viragadel6/minimaxh3 (read only)")
     ap.add_argument("--out", default=os.path.dirname(os.path.abspath(__file__)))
     args = ap.parse_args()
     _patch_interpreter()

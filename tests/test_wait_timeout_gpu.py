@@ -3,11 +3,12 @@
 Every mbarrier wait of the attention and GEMM kernels gives up after
 ``timeout_ns`` and records MH3_DEVERR_WAIT_TIMEOUT in the caller's error
 word; the CTA then drains the copies and MMAs already in flight (under a
-fixed bound of its own), frees its tensor memory and returns.  A launch with
-a 1 ns limit is a normal launch whose waits cannot be met in time: the test
-expects the error code, a clean return (no CUDA error) and a context that
-still computes the same bits on the next, normally bounded launch.  No
-trap, no bad address, no wait that nothing could end.
+fixed bound of its own), frees its tensor memory and returns.  The test sets
+MH3_TEST_STALL_PRODUCER, which makes each CTA's load warp first wait (with
+a 1 ms limit) on a barrier that nothing arrives on, and expects the error
+code, a clean return (no CUDA error) and a context that still computes the
+same bits on the next, normal launch.  No trap, no bad address; every wait
+has its limit.
 """
 import math
 
@@ -41,7 +42,8 @@ def test_attention_wait_timeout_sets_error_and_context_survives():
     good = ops.attention_e4m3(q8, k8, v16, sq, sk, sv, logit_scale_log2=ls2, err=err)
     torch.cuda.synchronize()
     assert int(err.item()) == 0
-    ops.attention_e4m3(q8, k8, v16, sq, sk, sv, logit_scale_log2=ls2, err=err, timeout_ns=1)
+    ops.attention_e4m3(q8, k8, v16, sq, sk, sv, logit_scale_log2=ls2, err=err, timeout_ns=1_000_000,
+                       test_flags=_lib.MH3_TEST_STALL_PRODUCER)
     torch.cuda.synchronize()  # a clean return: no CUDA error is raised here
     assert int(err.item()) == _lib.MH3_DEVERR_WAIT_TIMEOUT
     err.zero_()
@@ -51,18 +53,19 @@ def test_attention_wait_timeout_sets_error_and_context_survives():
     assert torch.equal(again, good)
 
 
-def test_gemm_wait_timeout_sets_error_and_context_survives():
+@pytest.mark.parametrize("M,N,K", [(4096, 5120, 2048), (64, 512, 1024)])  # CTA-pair and single-CTA kernels
+def test_gemm_wait_timeout_sets_error_and_context_survives(M, N, K):
     from minimaxh3_b200 import ops
 
     g = torch.Generator(device=DEV).manual_seed(10)
-    M, N, K = 4096, 5120, 2048
     x8, sa = ops.quantize_rows(torch.randn(M, K, generator=g, device=DEV).to(torch.bfloat16))
     w8, sb = ops.quantize_rows((torch.randn(N, K, generator=g, device=DEV) * 0.02).to(torch.bfloat16))
     err = torch.zeros(1, dtype=torch.int32, device=DEV)
     good = ops.scaled_gemm(x8, w8, row_scale=sa, col_scale=sb, err=err)
     torch.cuda.synchronize()
     assert int(err.item()) == 0
-    ops.scaled_gemm(x8, w8, row_scale=sa, col_scale=sb, err=err, timeout_ns=1)
+    ops.scaled_gemm(x8, w8, row_scale=sa, col_scale=sb, err=err, timeout_ns=1_000_000,
+                    test_flags=_lib.MH3_TEST_STALL_PRODUCER)
     torch.cuda.synchronize()
     assert int(err.item()) == _lib.MH3_DEVERR_WAIT_TIMEOUT
     err.zero_()
