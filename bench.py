@@ -46,6 +46,7 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 B, H, S, D = 1, 40, 32760, 128
+LOG2E_ = 1.4426950408889634
 NOMINAL_FP8_TFLOPS = 4500.0
 
 
@@ -331,6 +332,47 @@ def run_reference_arm(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def config5_single_gpu(dev, steps=3, warmup=1):
+    """Config 5's work on ONE GPU: S=75600 H=40 D=128 self-attention (per-(b,h) scales over the whole
+    sequence, e4m3 Q/K, f16 V/scale, the same quantisation kernels the sharded path runs) plus the
+    cross-attention of all 75600 tokens to 512 text tokens - the N=1 point of the sharded workload,
+    device-resident, timed with CUDA events."""
+    from minimaxh3_b200 import ops
+    from minimaxh3_b200.kernels.fp8_attention import fp8_attention
+
+    S5, H5, D5, T = 75600, 40, 128, 512
+    g = torch.Generator(device=dev).manual_seed(1000)
+    gc = torch.Generator().manual_seed(0)
+    xs = []
+    for _ in range(3):
+        x = torch.randn(1, S5, H5, D5, generator=g, device=dev)
+        x[..., int(torch.randperm(D5, generator=gc)[0])] *= 8.0
+        xs.append(x.to(torch.bfloat16))
+        del x
+    q, k, v = xs
+    gt = torch.Generator(device=dev).manual_seed(7)
+    kt, vt = (torch.randn(1, H5, T, D5, generator=gt, device=dev).to(torch.bfloat16) for _ in range(2))
+    ls2 = LOG2E_ / math.sqrt(D5)
+    out = torch.empty(1, S5, H5, D5, dtype=torch.bfloat16, device=dev)
+
+    def step():
+        amax = torch.stack([ops.absmax_bh(t) for t in (q, k, v)])        # [3, B, H]
+        sc = torch.clamp(amax, min=1e-12) / 448.0
+        q8 = ops.quantize_bh(q, sc[0])[0].transpose(1, 2)                 # [B, H, S, D] views
+        k8 = ops.quantize_bh(k, sc[1])[0].transpose(1, 2)
+        v16 = ops.quantize_bh(v, sc[2], out_dtype=torch.float16)[0].transpose(1, 2)
+        ops.attention_e4m3(q8, k8, v16, sc[0][..., None], sc[1][..., None], sc[2][..., None],
+                           logit_scale_log2=ls2, out=out.transpose(1, 2))
+        return fp8_attention(q.transpose(1, 2), kt, vt)
+
+    stream = torch.cuda.current_stream(dev)
+    ms = _time_cuda(step, steps, warmup, stream)
+    flop = 4.0 * H5 * S5 * S5 * D5 + 4.0 * H5 * S5 * T * D5
+    return {"workload": "config5 on one GPU: self-attention B=1 H=40 S=75600 D=128 + cross-attention to 512 "
+                        "tokens (no collectives)", "ms_per_step": ms, "value": flop / ms / 1e9, "unit": "TFLOP/s",
+            "steps": steps}
+
+
 def run_ulysses_arm(args, dist, rank, world, local):
     from minimaxh3_b200.kernels.fp8_attention import fp8_attention
     from minimaxh3_b200.ulysses import default_head_groups, ulysses_attention, ulysses_attention_host
@@ -407,6 +449,14 @@ def run_ulysses_arm(args, dist, rank, world, local):
     e2e_ms = float(t[0])
     if rank != 0:
         return
+    # The same workload on rank 0's GPU alone (no collectives), so the sharded value can be
+    # compared with its own N=1 point; the other ranks wait at the final barrier meanwhile.
+    torch.cuda.empty_cache()
+    try:
+        n1 = config5_single_gpu(dev)
+        n1["efficiency_of_this_line"] = value / (world * n1["value"])
+    except Exception as e:  # noqa: BLE001
+        n1 = {"unavailable": f"{type(e).__name__}: {str(e)[:300]}"}
     line = {
         "metric": "FP8 attention TFLOPS (S=32760 H=40 D=128)",
         "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -427,6 +477,7 @@ def run_ulysses_arm(args, dist, rank, world, local):
         # per step and head group: 3 absmax + 3 quantize_bh + 1 attention;
         # per step: the cross-attention's 5 quantisation kernels + 1 attention
         "gpu_launches": (7 * G + 6) * args.steps, "clocks": clk.summary(),
+        "n1_same_workload": n1,
     }
     print(json.dumps(line), flush=True)
 
@@ -585,7 +636,8 @@ def run_gpu_arm(args, dist, rank, world, local):
     extras = {}
     for name, fn in (("config4_linear", lambda: linear_results(32760, 5, 3)),
                      ("config3_varlen", lambda: varlen_results(5, 3)),
-                     ("dit_block", lambda: block_results(5, 3))):
+                     ("dit_block", lambda: block_results(5, 3)),
+                     ("config5_single_gpu", lambda: config5_single_gpu(dev))):
         try:
             extras[name] = fn()
         except Exception as e:  # noqa: BLE001

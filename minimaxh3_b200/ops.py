@@ -8,6 +8,7 @@ these paths.
 """
 from __future__ import annotations
 
+import collections
 import math
 
 import torch
@@ -468,7 +469,41 @@ def _round_up(x: int, m: int) -> int:
     return (x + m - 1) // m * m
 
 
-def _lora_operands(adapters, N: int, K: int, device, col_scale=None):
+# Folded LoRA operands, keyed on the identity and version of the adapter tensors and of the
+# column scale: a layer's forward reuses them until an adapter or the weight scale changes
+# (runtime/lora.py swaps the ``adapters`` list, an in-place edit bumps a tensor's version).
+# Entries hold the source tensors, so a key's ids cannot be reused while it is cached.
+_LORA_CACHE: "collections.OrderedDict" = collections.OrderedDict()
+_LORA_CACHE_MAX = 1024
+
+
+def _lora_key(adapters, scale_src):
+    parts = []
+    for A, B_, s in adapters:
+        parts += [id(A), A._version, id(B_), B_._version, float(s)]
+    if scale_src is not None:
+        parts += [id(scale_src), scale_src._version]
+    return tuple(parts)
+
+
+def _lora_operands(adapters, N: int, K: int, device, col_scale=None, scale_src=None):
+    """``_fold_lora`` with a cache over calls (see ``_LORA_CACHE``); ``scale_src`` is the tensor
+    ``col_scale`` was derived from (the layer's ``w_scale`` buffer), which keys the cache."""
+    scale_src = col_scale if scale_src is None else scale_src
+    key = _lora_key(adapters, scale_src)
+    hit = _LORA_CACHE.get(key)
+    if hit is not None:
+        _LORA_CACHE.move_to_end(key)
+        return hit[1], hit[2]
+    A_cat, B_cat = _fold_lora(adapters, N, K, device, col_scale)
+    refs = [t for A, B_, _ in adapters for t in (A, B_)] + ([scale_src] if scale_src is not None else [])
+    _LORA_CACHE[key] = (refs, A_cat, B_cat)
+    while len(_LORA_CACHE) > _LORA_CACHE_MAX:
+        _LORA_CACHE.popitem(last=False)
+    return A_cat, B_cat
+
+
+def _fold_lora(adapters, N: int, K: int, device, col_scale=None):
     """(A_cat [Rp, K] bf16, B_cat [N, Rp] bf16 = (scale*B)_cat / col_scale): the adapters
     concatenated along the rank (padded to a multiple of 16 with zeros)."""
     R = sum(int(A.shape[0]) for A, _, _ in adapters)
@@ -505,7 +540,7 @@ def fp8_linear(x2d: torch.Tensor, w8: torch.Tensor, w_scale: torch.Tensor, bias,
     a2 = b2 = None
     if adapters:
         xb = x2d if x2d.dtype == torch.bfloat16 else x2d.to(torch.bfloat16)
-        A_cat, b2 = _lora_operands(adapters, N, K, x2d.device, col_scale=sb)
+        A_cat, b2 = _lora_operands(adapters, N, K, x2d.device, col_scale=sb, scale_src=w_scale)
         a2 = scaled_gemm(xb, A_cat, row_scale=sa, row_scale_inv=True)
     return scaled_gemm(x8, w8, row_scale=sa, col_scale=sb, bias=bias, a2=a2, b2=b2)
 

@@ -41,3 +41,27 @@ def test_no_adapters_is_the_plain_forward_and_cpu_gets_two_step_lora():
     assert not fused_supported(lin, x)
     ref = x @ lin.weight.t() + lin.bias + 0.5 * ((x @ A.t()) @ B.t())
     assert torch.allclose(lin(x), ref, atol=1e-5)
+
+
+def test_folded_lora_operands_are_cached_until_an_input_changes():
+    """ops._lora_operands reuses the folded (A_cat, B_cat) of a layer until an adapter tensor,
+    its scale or the weight scale changes (an in-place edit bumps a tensor's version)."""
+    from minimaxh3_b200 import ops
+
+    g = torch.Generator().manual_seed(3)
+    A = torch.randn(8, 64, generator=g).to(torch.bfloat16)
+    Bm = torch.randn(32, 8, generator=g).to(torch.bfloat16)
+    ws = torch.rand(1, 32, generator=g) + 0.5
+    first = ops._lora_operands([(A, Bm, 1.0)], 32, 64, "cpu", col_scale=ws.reshape(-1), scale_src=ws)
+    again = ops._lora_operands([(A, Bm, 1.0)], 32, 64, "cpu", col_scale=ws.reshape(-1), scale_src=ws)
+    assert again[0] is first[0] and again[1] is first[1]
+    fresh = ops._fold_lora([(A, Bm, 1.0)], 32, 64, "cpu", col_scale=ws.reshape(-1))
+    assert torch.equal(fresh[0], first[0]) and torch.equal(fresh[1], first[1])
+    Bm.mul_(2.0)
+    edited = ops._lora_operands([(A, Bm, 1.0)], 32, 64, "cpu", col_scale=ws.reshape(-1), scale_src=ws)
+    assert edited[1] is not first[1] and not torch.equal(edited[1], first[1])
+    rescaled = ops._lora_operands([(A, Bm, 0.5)], 32, 64, "cpu", col_scale=ws.reshape(-1), scale_src=ws)
+    assert torch.equal(rescaled[1].float(), (edited[1].float() * 0.5).to(torch.bfloat16).float())
+    ws.mul_(2.0)
+    new_scale = ops._lora_operands([(A, Bm, 0.5)], 32, 64, "cpu", col_scale=ws.reshape(-1), scale_src=ws)
+    assert new_scale[1] is not rescaled[1]
