@@ -12,8 +12,9 @@
 //  * mh3_quantize_rows: per-row scales for the FP8 linear
 //    (kernels/fp8_linear.py:8-42).
 //
-// Divisions are IEEE round-to-nearest (``__fdiv_rn``) and the e4m3 cast is
-// RNE after the same +-448 clamp, so the bytes match the CPU restatement.
+// Quotients are correctly rounded (IEEE round-to-nearest, see div_rn_by) and
+// the e4m3 cast is RNE with saturation at +-448 (the reference's clamp), so
+// the bytes match the CPU restatement.
 #include <mutex>
 
 #include "mh3_internal.h"
@@ -72,6 +73,22 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
 }
 
 __device__ __forceinline__ float clamp448(float x) { return fminf(fmaxf(x, -448.0f), 448.0f); }
+
+// x / s rounded to nearest even, given r = 1/s rounded to nearest (``__frcp_rn``,
+// once per scale): Markstein's correction step - q = x*r, the remainder
+// e = x - s*q is exact in one FMA, q + e*r rounds to the correctly rounded
+// quotient (P. Markstein, "Computation of elementary functions on the IBM
+// RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990; also the
+// "Handbook of Floating-Point Arithmetic", ch. on division).  Holds while the
+// quotient is a normal float; the quotients here are at most 448 in
+// magnitude, and ones too small to be normal round to 0 in e4m3 and f16 alike.
+// Three FMA-pipe operations where an IEEE division takes about ten: the
+// quantisation kernels are otherwise issue-bound rather than HBM-bound.
+__device__ __forceinline__ float div_rn_by(float x, float s, float r) {
+  const float q = x * r;
+  const float e = fmaf(-s, q, x);
+  return fmaf(e, r, q);
+}
 
 // 8 floats -> 8 e4m3 bytes (element 0 in the lowest byte).
 __device__ __forceinline__ uint2 pack8_e4m3(const float (&y)[8]) {
@@ -188,10 +205,14 @@ __global__ void __launch_bounds__(kThreads, 3) block_quant_kernel(const T* __res
     const int row = blk * kBlockRows + rl + r * RL;
     raw[r] = row < S ? __ldg(reinterpret_cast<const uint4*>(xp + (long long)row * ss)) : make_uint4(0u, 0u, 0u, 0u);
   }
-  float c8[8];
+  float c8[8], r8[8];
   if (MODE != kQ) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) c8[i] = __ldg(chan + bh * D + cg * 8 + i);
+  }
+  if (MODE == kV) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r8[i] = __frcp_rn(c8[i]);
   }
   // transform (masked rows are 0, fp8_attention.py:69, :111)
   auto value = [&](int r, float (&v)[8]) {
@@ -217,6 +238,7 @@ __global__ void __launch_bounds__(kThreads, 3) block_quant_kernel(const T* __res
     s = fmaxf(bm, 1.0e-12f) / 448.0f;                  // :71, :113
     if (threadIdx.x == 0) scale[bh * nblk + blk] = s;
   }
+  const float rs = __frcp_rn(s);
   // Convert again from the raw pieces instead of keeping R*8 floats alive
   // across the reduction (the empty asm hides the first conversion from CSE).
 #pragma unroll
@@ -230,7 +252,13 @@ __global__ void __launch_bounds__(kThreads, 3) block_quant_kernel(const T* __res
       float y[8];
       value(r, y);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) y[i] = clamp448(__fdiv_rn(y[i], MODE == kV ? c8[i] : s));  // :72, :114, :167
+      // divide (:72, :114, :167); the +-448 clamp is cvt.satfinite's for e4m3
+      for (int i = 0; i < 8; ++i)
+        y[i] = MODE == kV ? div_rn_by(y[i], c8[i], r8[i]) : div_rn_by(y[i], s, rs);
+      if constexpr (OUT_F16) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = clamp448(y[i]);
+      }
       if constexpr (OUT_F16) {
         uint4 u;
         u.x = cvt_f16x2(y[1], y[0]);
@@ -260,13 +288,14 @@ __global__ void __launch_bounds__(kThreads) rows_quant_kernel(const T* __restric
     for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
   }
   const float s = fmaxf(block_max(amax, red), 1.0e-12f) / 448.0f;   // :20-21
+  const float rs = __frcp_rn(s);
   if (threadIdx.x == 0) scale[row] = s;
   uint8_t* op = x8 + row * K;
   for (int c = threadIdx.x * 8; c < K; c += kThreads * 8) {
     float v[8], y[8];
     load8(xp + c, v);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) y[i] = clamp448(__fdiv_rn(v[i], s));   // :22
+    for (int i = 0; i < 8; ++i) y[i] = div_rn_by(v[i], s, rs);   // :22 (clamp: cvt.satfinite)
     *reinterpret_cast<uint2*>(op + c) = pack8_e4m3(y);
   }
 }
@@ -303,6 +332,7 @@ __global__ void __launch_bounds__(NT) rows_quant_reg_kernel(const T* __restrict_
 #pragma unroll
   for (int i = 1; i < NT / 32; ++i) bm = fmaxf(bm, red[i]);
   const float s = fmaxf(bm, 1.0e-12f) / 448.0f;   // fp8_linear.py:20-21
+  const float rs = __frcp_rn(s);
   if (threadIdx.x == 0) scale[row] = s;
   uint8_t* op = x8 + row * K;
 #pragma unroll
@@ -312,7 +342,7 @@ __global__ void __launch_bounds__(NT) rows_quant_reg_kernel(const T* __restrict_
       float v[8], y[8];
       unpack8<T>(raw[r], v);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) y[i] = clamp448(__fdiv_rn(v[i], s));   // :22
+      for (int i = 0; i < 8; ++i) y[i] = div_rn_by(v[i], s, rs);   // :22 (clamp: cvt.satfinite)
       *reinterpret_cast<uint2*>(op + c) = pack8_e4m3(y);
     }
   }
@@ -454,9 +484,10 @@ __global__ void __launch_bounds__(kThreads) bh_quant_kernel(const T* __restrict_
     float v[8];
     load8(x + b * sb + (long long)s * ss + h * sh + g * 8, v);
     const float sc = __ldg(scale + (long long)b * nsel + j);
+    const float rc = __frcp_rn(sc);
     float y[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) y[k] = OUT_F16 ? __fdiv_rn(v[k], sc) : clamp448(__fdiv_rn(v[k], sc));
+    for (int k = 0; k < 8; ++k) y[k] = div_rn_by(v[k], sc, rc);  // e4m3: clamp by cvt.satfinite
     const int p = j / sel.hs, hl = j - p * sel.hs;
     const long long o = ((((long long)p * B + b) * S + s) * sel.hs + hl) * D + g * 8;
     if constexpr (OUT_F16) {

@@ -89,3 +89,36 @@ def test_quantize_rows_golden():
         t8, ts = ops.quantize_rows(g[nm].to(DEV))
         assert torch.equal(t8.cpu().view(torch.uint8), g[nm + "8"])
         assert torch.equal(ts.cpu(), g[nm + "_scale"])
+
+
+def _wide(seed, shape, dtype=torch.bfloat16):
+    """N(0,1) scaled by 2^u with u uniform in [-24, 24): values across ~48 binades, so that the
+    quotients x/s fall on every mantissa pattern, with many near rounding midpoints of e4m3/f16."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(*shape, generator=g) * torch.exp2(torch.randint(-24, 24, shape, generator=g).float())
+    return x.to(dtype)
+
+
+def test_quotients_are_correctly_rounded_on_wide_ranges():
+    """The kernels divide by a scale through a reciprocal and one correction step; the bytes must
+    equal the restatement's IEEE division on data spanning many binades: e4m3 rows, the f16 V
+    operand (11-bit mantissa: sensitive to any misrounded quotient) and e4m3 Q/K blocks."""
+    from minimaxh3_b200 import ops
+
+    x = _wide(21, (2048, 4096))
+    x8, s = ops.quantize_rows(x.to(DEV))
+    r8, rs = OL.quantize_rows(x)
+    assert torch.equal(s.cpu(), rs)
+    assert torch.equal(x8.cpu().view(torch.uint8), r8.view(torch.uint8))
+    B, H, S, D = 1, 4, 8192, 128
+    q, k, v = (_wide(22 + i, (B, H, S, D)) for i in range(3))
+    q8, k8, v16, sq, sk, sv, km = (t.cpu() for t in ops.quantize_qkv(q.to(DEV), k.to(DEV), v.to(DEV), 0.1275,
+                                                                     v_dtype=torch.float16))
+    rsv = torch.clamp(v.float().abs().amax(dim=2), min=1e-12) / 448.0
+    assert torch.equal(sv, rsv)
+    rv16 = torch.clamp(v.float() / rsv[:, :, None, :], -448, 448).to(torch.float16)
+    assert torch.equal(v16.view(torch.int16), rv16.view(torch.int16))
+    rq8, rsq = OA.quantize_q(q, 0.1275)
+    assert torch.equal(sq, rsq) and torch.equal(q8.view(torch.uint8), rq8.view(torch.uint8))
+    rk8, rsk = OA.quantize_k(k, km[:, :, None])
+    assert torch.equal(sk, rsk) and torch.equal(k8.view(torch.uint8), rk8.view(torch.uint8))
