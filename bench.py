@@ -22,6 +22,15 @@ over H/N heads, bf16 all-to-all back), then cross-attention of the local
 query shard to 512 replicated text tokens.  ``value`` = total FLOPs of both
 attentions / max-over-ranks device time ("strong" scaling: total work fixed).
 
+The N=1 line also carries, measured after its timed regions on the same
+box: ``competitor_same_box`` - the reference's own Triton attention
+(``_fp8_attn_kernel`` alone, and ``fp8_attention`` end to end, from the
+unmodified copy that baseline/install_reference.py places in baseline/_ref)
+against this package's, 3 warm-ups then the median of 20; and ``extras`` -
+config 4 (FP8 linear, incl. the reference's ``FP8Linear`` module), config 3
+(varlen), a synthetic DiT block and config 5 on one GPU.  The N>1 line
+carries config 5 on rank 0's GPU alone (``n1_same_workload``).
+
 ``--impl reference``: the reference's CPU implementation of this path
 (``routed_sdpa`` falling back to torch SDPA on CPU tensors,
 kernels/attention_router.py:93-102) on rank 0's host cores, on a bounded
@@ -863,6 +872,8 @@ def run_quant_workload(args):
     """
     from minimaxh3_b200 import ops
 
+    global H
+    H = args.heads  # 40 = config 2; fewer for ncu captures
     dev = torch.device("cuda", 0)
     stream = torch.cuda.current_stream(dev)
     q, k, v = _synthetic_qkv(dev)
@@ -877,7 +888,7 @@ def run_quant_workload(args):
         lines.append({"v_out": str(vd).replace("torch.", ""), "ms": ms, "algorithmic_bytes": algo,
                       "achieved_gbs": algo / ms / 1e6, "frac_of_hbm": algo / ms / 1e6 / peaks["hbm_gbs"],
                       "bytes_moved": moved, "moved_gbs": moved / ms / 1e6})
-    print(json.dumps({"workload": "config2 drop-in quantisation: bf16 q,k,v [1,40,32760,128] -> e4m3 + scales",
+    print(json.dumps({"workload": f"config2 drop-in quantisation: bf16 q,k,v [1,{H},32760,128] -> e4m3 + scales",
                       "unit": "GB/s", "peak_hbm_gbs": peaks["hbm_gbs"], "results": lines}), flush=True)
 
 
