@@ -287,3 +287,51 @@ def test_padded_batch_kv_len_skips_tiles_exactly(pv):
     ref = OA.sdpa_dequant_oracle(q8.double() * sq[..., None, None], k8.double() * sk[..., None, None],
                                  v8.double() * sv[..., None, None], ls2, key_mask=key_mask, base2=True)
     _check(OA.compare(skip.float().cpu(), ref), pv)
+
+
+@pytest.mark.parametrize("pv", ["f16", "e4m3"])
+def test_attention_varlen_empty_and_one_token_sequences(pv):
+    """Packed sequences of 0 and 1 tokens, and different query / key packings (cross-attention):
+    a sequence with no queries writes nothing, one with no keys gives 0, the rest match the oracle."""
+    from minimaxh3_b200 import ops
+
+    H, D = 2, 128
+    lq, lk = [5, 0, 130, 1, 64], [0, 7, 300, 1, 129]
+    g = torch.Generator().manual_seed(11)
+    cq = torch.tensor([0] + list(torch.tensor(lq).cumsum(0)), dtype=torch.int32)
+    ck = torch.tensor([0] + list(torch.tensor(lk).cumsum(0)), dtype=torch.int32)
+    q = torch.randn(int(cq[-1]), H, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(int(ck[-1]), H, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(int(ck[-1]), H, D, generator=g).to(torch.bfloat16)
+
+    def quant(t, cu):
+        t8 = torch.empty(t.shape, dtype=torch.float8_e4m3fn)
+        sc = torch.ones(len(cu) - 1, H, 1)
+        for i in range(len(cu) - 1):
+            sl = slice(int(cu[i]), int(cu[i + 1]))
+            if sl.stop > sl.start:
+                s = torch.clamp(t[sl].float().abs().amax(dim=(0, 2)), min=1e-12) / 448.0
+                sc[i, :, 0] = s
+                t8[sl] = torch.clamp(t[sl].float() / s[None, :, None], -448, 448).to(torch.float8_e4m3fn)
+        return t8, sc
+
+    (q8, sq), (k8, sk), (v8, sv) = quant(q, cq), quant(k, ck), quant(v, ck)
+    ls2 = OA.LOG2E / math.sqrt(D)
+    vd = v8.to(DEV)
+    if pv == "f16":
+        vd = ops.widen_e4m3_to_f16(vd)
+    out = torch.full((int(cq[-1]), H, D), 7.0, dtype=torch.bfloat16, device=DEV)
+    ops.attention_e4m3(q8.to(DEV), k8.to(DEV), vd, sq.to(DEV), sk.to(DEV), sv.to(DEV), logit_scale_log2=ls2,
+                       cu_seqlens_q=cq.to(DEV), cu_seqlens_k=ck.to(DEV), max_seqlen_q=max(lq), out=out)
+    out = out.float().cpu()
+    for i in range(len(lq)):
+        qs, ks = slice(int(cq[i]), int(cq[i + 1])), slice(int(ck[i]), int(ck[i + 1]))
+        if lq[i] == 0:
+            continue
+        if lk[i] == 0:
+            assert torch.equal(out[qs], torch.zeros_like(out[qs])), i
+            continue
+        qi, ki, vi = (t.permute(1, 0, 2)[None] for t in (q8[qs], k8[ks], v8[ks]))
+        ref = OA.sdpa_dequant_oracle(qi.double() * sq[i][None, :, :, None], ki.double() * sk[i][None, :, :, None],
+                                     vi.double() * sv[i][None, :, :, None], ls2, base2=True)
+        _check(OA.compare(out[qs].permute(1, 0, 2)[None], ref), pv)
