@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mh3|reference]
 
-Default arm (``--impl mh3``), N=1: BASELINE config 2 - FP8 self-attention
+Default arm (``--impl mh3``), N=1: benchmark configuration 2 - FP8 self-attention
 forward, B=1 H=40 S=32760 D=128, e4m3 q/k/v with per-(batch, head) scales
 (synthetic N(0,1) with one of 128 channels x8, seed 0), bf16 out.  With the
 default 16-bit PV product (``--pv f16``) a step is one exact e4m3->f16
@@ -15,7 +15,7 @@ larger than the 126 MB L2).  ``e2e`` times
 attended by the drop-in ``fp8_attention``, and copied back, with the three
 stages overlapping on separate streams.
 
-N>1 (torchrun): BASELINE config 5, the sharded configuration - S=75600 H=40
+N>1 (torchrun): benchmark configuration 5, the sharded configuration - S=75600 H=40
 D=128 self-attention with Ulysses head parallelism (per-(b,h) scales
 all-reduced, e4m3 q/k and f16 v all-to-all over NCCL, local FP8 attention
 over H/N heads, bf16 all-to-all back), then cross-attention of the local
@@ -179,7 +179,7 @@ def _reference_kernels():
 
 
 def _median_ms(fn, stream, warmup=3, reps=20):
-    """BASELINE.md's competitor protocol: warm-ups, then the median of CUDA-event timings."""
+    """The competitor protocol: warm-ups, then the median of CUDA-event timings."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -196,7 +196,7 @@ def _median_ms(fn, stream, warmup=3, reps=20):
 
 
 def triton_competitor(q, k, v, stream):
-    """The reference's GPU path on the same box and inputs (BASELINE.md competitor 1).
+    """The reference's GPU path on the same box and inputs (the first named competitor).
 
     (i) ``_fp8_attn_kernel`` alone - autotuned, warp-specialised on cc 10 - on
     the operands its own wrapper makes (kernels/fp8_attention.py:300-402),
@@ -675,7 +675,7 @@ def run_linear_workload(args):
 
 
 def linear_results(M, steps, warmup):
-    """FP8 scaled linear with fused epilogue (not the headline).
+    """Benchmark configuration 4: FP8 scaled linear with fused epilogue (not the headline).
 
     M=32760 tokens, K=5120, N in {5120, 15360, 13824}; x N(0,1) bf16, W N(0,0.02),
     bias N(0,0.01), one LoRA adapter of rank 32 (A, B ~ N(0,0.01), scale 1).
@@ -769,7 +769,7 @@ def run_varlen_workload(args):
 
 
 def varlen_results(steps, warmup):
-    """packed varlen, cu_seqlens [0, 33784, 50676], H=40 D=128.
+    """Benchmark configuration 3: packed varlen, cu_seqlens [0, 33784, 50676], H=40 D=128.
 
     e4m3 q/k/v with per-(sequence, head) scales (synthetic N(0,1) with one
     channel x8), f16 PV, bf16 out; attention is block-diagonal per sequence.
@@ -803,11 +803,25 @@ def varlen_results(steps, warmup):
     call = lambda: ops.attention_e4m3(q8, k8, v16, *scales, logit_scale_log2=ls2, cu_seqlens_q=cu,
                                       cu_seqlens_k=cu, max_seqlen_q=max(lens), out=out)
     ms = _time_cuda(call, steps, warmup, stream)
+    del q8, k8, v16, out
+    # the drop-in route: bf16 packed q/k/v -> per-(sequence, head) quantisation + the same kernel
+    from minimaxh3_b200.kernels.fp8_attention import fp8_attention_varlen
+
+    qkv = []
+    for _ in range(3):
+        x = torch.randn(T, Hh, Dd, generator=g, device=dev, dtype=torch.bfloat16)
+        x[..., int(torch.randperm(Dd, generator=gc)[0])] *= 8.0
+        qkv.append(x)
+    dropin = lambda: fp8_attention_varlen(*qkv, cu, cu, max(lens))
+    ms_dropin = _time_cuda(dropin, steps, warmup, stream)
+    del qkv
     flop = 4.0 * Hh * Dd * sum(L * L for L in lens)
     peaks = _peaks()
     return {"workload": "config3: varlen cu_seqlens [0,33784,50676], H=40 D=128, per-(seq,head) "
                         "scales, f16 PV", "unit": "TFLOP/s", "ms": ms, "tflops": flop / ms / 1e9,
-            "frac_of_fp8_peak": flop / ms / 1e9 / peaks["fp8_tflops"], "flop": flop}
+            "frac_of_fp8_peak": flop / ms / 1e9 / peaks["fp8_tflops"], "flop": flop,
+            "dropin_ms": ms_dropin, "dropin_tflops": flop / ms_dropin / 1e9,
+            "dropin": "fp8_attention_varlen: bf16 packed q/k/v, mh3_absmax_seg + mh3_quantize_seg + attention"}
 
 
 def run_block_workload(args):

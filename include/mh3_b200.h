@@ -36,8 +36,8 @@ extern "C" {
  * 2: mh3_attn_args.kv_len; 3: head selection in mh3_absmax_bh /
  * mh3_quantize_bh, mh3_copy_rows, mh3_step_diff; 4: f32 input to
  * mh3_quantize_rows, test_flags in mh3_attn_args (was reserved0) and
- * mh3_gemm_args. */
-#define MH3_ABI_VERSION 4
+ * mh3_gemm_args; 5: mh3_absmax_seg, mh3_quantize_seg. */
+#define MH3_ABI_VERSION 5
 
 #define MH3_OK 0
 #define MH3_ERR_INVALID (-1)     /* bad argument: shape, stride, alignment, null pointer */
@@ -262,7 +262,7 @@ MH3_API int mh3_scaled_gemm(const mh3_gemm_args* args, void* stream);
 MH3_API int mh3_widen_e4m3_to_f16(const void* src, void* dst, int64_t n, void* stream);
 
 /* ------------------------------------------------------------------------ */
-/* Per-(batch, head) quantisation (BASELINE configs 2/3/5 scale granularity) */
+/* Per-(batch, head) quantisation (the scale granularity of the benchmark workloads) */
 /* ------------------------------------------------------------------------ */
 /*
  * The per-(batch, head) form of the reference's Q/K/V quantisation
@@ -288,6 +288,31 @@ MH3_API int mh3_absmax_bh(const void* x, int32_t in_dtype, int64_t B, int64_t S,
 MH3_API int mh3_quantize_bh(const void* x, int32_t in_dtype, int64_t B, int64_t S, int64_t H, int64_t D, int64_t sb,
                             int64_t ss, int64_t sh, int32_t head_block, int32_t head_off, int32_t heads_sel,
                             const float* scale, int32_t out_dtype, void* out, void* stream);
+
+/*
+ * Per-(segment, head) variants for packed variable-length batches (the
+ * cu_seqlens layout of the varlen attention): x is one packed [S, H, D]
+ * shard (token stride ss, head stride sh, elements) whose rows
+ * [seg[z], seg[z+1]) form segment z, z < nseg.  ``seg`` is int32 [nseg+1]
+ * on the device, non-decreasing; each entry is clamped to [0, S], so a
+ * sequence-parallel rank may pass the global cu_seqlens shifted by its first
+ * token.  Head selection as above.
+ *
+ * mh3_absmax_seg: amax[z*nsel+j] = max |x[rows of z, head(j), :]| (f32,
+ * overwritten; 0 for an empty segment).
+ * mh3_quantize_seg: y = x / scale[z*nsel+j] for the rows of segment z, as
+ * mh3_quantize_bh with B = 1: out [P, S, heads_sel, D] contiguous.  Rows
+ * outside every segment are written as zeros.
+ * No reference counterpart: the reference has no varlen path.  These give
+ * the per-(sequence, head) absmax/448 scales of the packed video+audio
+ * workload, on one GPU or across sequence-parallel ranks.
+ */
+MH3_API int mh3_absmax_seg(const void* x, int32_t in_dtype, int64_t S, int64_t H, int64_t D, int64_t ss, int64_t sh,
+                           int32_t head_block, int32_t head_off, int32_t heads_sel, const int32_t* seg, int32_t nseg,
+                           float* amax, void* stream);
+MH3_API int mh3_quantize_seg(const void* x, int32_t in_dtype, int64_t S, int64_t H, int64_t D, int64_t ss, int64_t sh,
+                             int32_t head_block, int32_t head_off, int32_t heads_sel, const int32_t* seg,
+                             int32_t nseg, const float* scale, int32_t out_dtype, void* out, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Strided host<->device row copies                                         */

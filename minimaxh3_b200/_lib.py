@@ -99,6 +99,10 @@ _SIGNATURES = {
                               c_ptr, c_ptr]),
     "mh3_quantize_bh": (c_i32, [c_ptr, c_i32, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i32, c_i32, c_i32,
                                 c_ptr, c_i32, c_ptr, c_ptr]),
+    "mh3_absmax_seg": (c_i32, [c_ptr, c_i32, c_i64, c_i64, c_i64, c_i64, c_i64, c_i32, c_i32, c_i32, c_ptr, c_i32,
+                               c_ptr, c_ptr]),
+    "mh3_quantize_seg": (c_i32, [c_ptr, c_i32, c_i64, c_i64, c_i64, c_i64, c_i64, c_i32, c_i32, c_i32, c_ptr, c_i32,
+                                 c_ptr, c_i32, c_ptr, c_ptr]),
     "mh3_copy_rows": (c_i32, [c_ptr, c_i64, c_ptr, c_i64, c_i64, c_i64, c_ptr]),
     "mh3_step_diff_workspace_bytes": (c_u64, []),
     "mh3_step_diff": (c_i32, [c_ptr, c_ptr, c_i32, c_i64, c_i32, c_ptr, c_ptr, c_ptr]),

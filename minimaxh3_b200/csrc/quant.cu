@@ -434,22 +434,50 @@ struct HeadSel {
   __device__ __forceinline__ int head(int j) const { return (j / hs) * hb + off + j % hs; }
 };
 
+// Segments of a packed shard: x is [S, H, D] (B = 1) and its rows
+// [seg[z], seg[z+1]) form segment z (seg non-decreasing, each entry clamped
+// to [0, S]); the per-segment kernels below index scales by z where the
+// per-batch ones index them by b.
+struct Segs {
+  const int* seg;
+  int nseg;
+  __device__ __forceinline__ int bound(int z, int S) const { return min(max(__ldg(seg + z), 0), S); }
+  // The segment holding row s, or -1 when s lies outside every segment.
+  __device__ __forceinline__ int find(int s, int S) const {
+    if (s < bound(0, S) || s >= bound(nseg, S)) return -1;
+    int lo = 0, hi = nseg - 1;                 // largest z with bound(z) <= s
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (bound(mid, S) <= s) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+  }
+};
+
 // Per-(batch, head) absmax of x [B, S, H, D] (element strides sb/ss/sh, D
 // contiguous) over the selected heads: one CTA per (256-row chunk, j, b),
 // CTA max folded into amax[b*nsel+j] with an integer atomicMax (non-negative
-// floats order like their bit patterns; amax starts at 0).
-template <typename T, int D>
+// floats order like their bit patterns; amax starts at 0).  SEG: b is a
+// segment z of a packed [S, H, D] shard and the chunks start at its first row.
+template <typename T, int D, bool SEG>
 __global__ void __launch_bounds__(kThreads) bh_absmax_kernel(const T* __restrict__ x, long long sb, long long ss,
-                                                            long long sh, int S, HeadSel sel, float* __restrict__ amax) {
+                                                            long long sh, int S, HeadSel sel, Segs segs,
+                                                            float* __restrict__ amax) {
   constexpr int CG = D / 8;
   constexpr int RL = kThreads / CG;
   __shared__ float red[kThreads / 32];
   const int j = blockIdx.y, b = blockIdx.z;
   const int h = sel.head(j);
   const int cg = threadIdx.x % CG, rl = threadIdx.x / CG;
-  const T* xp = x + b * sb + h * sh + cg * 8;
-  const int r0 = blockIdx.x * kStatRows;
-  const int r1 = min(S, r0 + kStatRows);
+  int first = 0, last = S;
+  if constexpr (SEG) {
+    first = segs.bound(b, S);
+    last = max(first, segs.bound(b + 1, S));
+  }
+  const int r0 = first + blockIdx.x * kStatRows;
+  if (r0 >= last) return;                       // uniform over the CTA
+  const int r1 = min(last, r0 + kStatRows);
+  const T* xp = x + (SEG ? 0 : b * sb) + h * sh + cg * 8;
   float m = 0.0f;
   for (int r = r0 + rl; r < r1; r += RL) {
     float v[8];
@@ -465,11 +493,13 @@ __global__ void __launch_bounds__(kThreads) bh_absmax_kernel(const T* __restrict
 // to +-448, RNE) or f16 (RNE), written block-major: out [P, B, S, hs, D] with
 // P = H/hb and selected head j = p*hs + i at [p, b, s, i] - the send buffer of
 // a head-parallel all-to-all (all heads, hb = H: plain [B, S, H, D]).  One
-// thread per 8 channels.
-template <typename T, bool OUT_F16>
+// thread per 8 channels.  SEG (B = 1): row s takes the scale of its segment
+// z, scale[z, j]; rows outside every segment are written as zeros.
+template <typename T, bool OUT_F16, bool SEG>
 __global__ void __launch_bounds__(kThreads) bh_quant_kernel(const T* __restrict__ x, long long sb, long long ss,
                                                            long long sh, int B, int S, int H, int D, HeadSel sel,
-                                                           const float* __restrict__ scale, uint8_t* __restrict__ out) {
+                                                           Segs segs, const float* __restrict__ scale,
+                                                           uint8_t* __restrict__ out) {
   const int CG = D / 8;
   const int nsel = (H / sel.hb) * sel.hs;
   const long long n = (long long)B * S * nsel * CG;
@@ -481,13 +511,19 @@ __global__ void __launch_bounds__(kThreads) bh_quant_kernel(const T* __restrict_
     const int s = (int)(t % S);
     const int b = (int)(t / S);
     const int h = sel.head(j);
-    float v[8];
-    load8(x + b * sb + (long long)s * ss + h * sh + g * 8, v);
-    const float sc = __ldg(scale + (long long)b * nsel + j);
-    const float rc = __frcp_rn(sc);
+    const int z = SEG ? segs.find(s, S) : b;
     float y[8];
+    if (z >= 0) {
+      float v[8];
+      load8(x + b * sb + (long long)s * ss + h * sh + g * 8, v);
+      const float sc = __ldg(scale + (long long)z * nsel + j);
+      const float rc = __frcp_rn(sc);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) y[k] = div_rn_by(v[k], sc, rc);  // e4m3: clamp by cvt.satfinite
+      for (int k = 0; k < 8; ++k) y[k] = div_rn_by(v[k], sc, rc);  // e4m3: clamp by cvt.satfinite
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) y[k] = 0.0f;
+    }
     const int p = j / sel.hs, hl = j - p * sel.hs;
     const long long o = ((((long long)p * B + b) * S + s) * sel.hs + hl) * D + g * 8;
     if constexpr (OUT_F16) {
@@ -536,8 +572,9 @@ extern "C" int mh3_absmax_bh(const void* x, int32_t in_dtype, int64_t B, int64_t
   if (e != cudaSuccess) return fail_cuda(e, "mh3_absmax_bh memset");
   const dim3 grid((unsigned)((S + quant::kStatRows - 1) / quant::kStatRows), (unsigned)nsel, (unsigned)B);
   if (grid.x > 2147483647u) return fail(MH3_ERR_TOO_LARGE, "mh3_absmax_bh: too many rows");
-#define MH3_ABSMAX(T, DD) \
-  quant::bh_absmax_kernel<T, DD><<<grid, quant::kThreads, 0, st>>>(static_cast<const T*>(x), sb, ss, sh, (int)S, sel, amax)
+#define MH3_ABSMAX(T, DD)                                                                                         \
+  quant::bh_absmax_kernel<T, DD, false><<<grid, quant::kThreads, 0, st>>>(static_cast<const T*>(x), sb, ss, sh, (int)S, \
+                                                                         sel, quant::Segs{nullptr, 0}, amax)
   if (in_dtype == MH3_DTYPE_BF16) {
     if (D == 128) MH3_ABSMAX(__nv_bfloat16, 128); else MH3_ABSMAX(__nv_bfloat16, 64);
   } else {
@@ -564,9 +601,9 @@ extern "C" int mh3_quantize_bh(const void* x, int32_t in_dtype, int64_t B, int64
   const long long n = B * S * (H / head_block) * heads_sel * (D / 8);
   const int blocks = (int)std::min<long long>((n + quant::kThreads - 1) / quant::kThreads, 148ll * 16);
   uint8_t* o = static_cast<uint8_t*>(out);
-#define MH3_BHQ(T, F16)                                                                                            \
-  quant::bh_quant_kernel<T, F16><<<blocks, quant::kThreads, 0, st>>>(static_cast<const T*>(x), sb, ss, sh, (int)B, \
-                                                                      (int)S, (int)H, (int)D, sel, scale, o)
+#define MH3_BHQ(T, F16)                                                                                      \
+  quant::bh_quant_kernel<T, F16, false><<<blocks, quant::kThreads, 0, st>>>(                                   \
+      static_cast<const T*>(x), sb, ss, sh, (int)B, (int)S, (int)H, (int)D, sel, quant::Segs{nullptr, 0}, scale, o)
   const bool f16 = out_dtype == MH3_DTYPE_F16;
   if (in_dtype == MH3_DTYPE_BF16) {
     if (f16) MH3_BHQ(__nv_bfloat16, true); else MH3_BHQ(__nv_bfloat16, false);
@@ -576,6 +613,71 @@ extern "C" int mh3_quantize_bh(const void* x, int32_t in_dtype, int64_t B, int64
 #undef MH3_BHQ
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? MH3_OK : fail_cuda(e, "mh3_quantize_bh launch");
+}
+
+extern "C" int mh3_absmax_seg(const void* x, int32_t in_dtype, int64_t S, int64_t H, int64_t D, int64_t ss,
+                              int64_t sh, int32_t head_block, int32_t head_off, int32_t heads_sel, const int32_t* seg,
+                              int32_t nseg, float* amax, void* stream) {
+  const char* why = nullptr;
+  if (!bh_shape_ok(x, in_dtype, 1, S, H, D, 0, ss, sh, &why)) return fail(MH3_ERR_INVALID, (std::string("mh3_absmax_seg: ") + why).c_str());
+  if (amax == nullptr || seg == nullptr) return fail(MH3_ERR_INVALID, "mh3_absmax_seg: null amax or seg");
+  if (nseg <= 0 || nseg > 65535) return fail(MH3_ERR_INVALID, "mh3_absmax_seg: nseg must be in [1, 65535]");
+  if (head_block <= 0 || H % head_block || head_off < 0 || heads_sel <= 0 || head_off + heads_sel > head_block)
+    return fail(MH3_ERR_INVALID, "mh3_absmax_seg: bad head selection");
+  const quant::HeadSel sel{head_block, head_off, heads_sel};
+  const int64_t nsel = (H / head_block) * heads_sel;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(amax, 0, (size_t)(nseg * nsel) * sizeof(float), st);
+  if (e != cudaSuccess) return fail_cuda(e, "mh3_absmax_seg memset");
+  // Each segment gets as many chunks as the whole shard has (its own length is
+  // only known on the device); chunks past a segment's end return at once.
+  const dim3 grid((unsigned)((S + quant::kStatRows - 1) / quant::kStatRows), (unsigned)nsel, (unsigned)nseg);
+  const quant::Segs segs{seg, nseg};
+#define MH3_ABSMAX(T, DD)                                                                                        \
+  quant::bh_absmax_kernel<T, DD, true><<<grid, quant::kThreads, 0, st>>>(static_cast<const T*>(x), 0, ss, sh, (int)S, \
+                                                                         sel, segs, amax)
+  if (in_dtype == MH3_DTYPE_BF16) {
+    if (D == 128) MH3_ABSMAX(__nv_bfloat16, 128); else MH3_ABSMAX(__nv_bfloat16, 64);
+  } else {
+    if (D == 128) MH3_ABSMAX(__half, 128); else MH3_ABSMAX(__half, 64);
+  }
+#undef MH3_ABSMAX
+  e = cudaGetLastError();
+  return e == cudaSuccess ? MH3_OK : fail_cuda(e, "mh3_absmax_seg launch");
+}
+
+extern "C" int mh3_quantize_seg(const void* x, int32_t in_dtype, int64_t S, int64_t H, int64_t D, int64_t ss,
+                                int64_t sh, int32_t head_block, int32_t head_off, int32_t heads_sel,
+                                const int32_t* seg, int32_t nseg, const float* scale, int32_t out_dtype, void* out,
+                                void* stream) {
+  const char* why = nullptr;
+  if (!bh_shape_ok(x, in_dtype, 1, S, H, D, 0, ss, sh, &why)) return fail(MH3_ERR_INVALID, (std::string("mh3_quantize_seg: ") + why).c_str());
+  if (scale == nullptr || out == nullptr || seg == nullptr)
+    return fail(MH3_ERR_INVALID, "mh3_quantize_seg: null scale, out or seg");
+  if (nseg <= 0 || nseg > 65535) return fail(MH3_ERR_INVALID, "mh3_quantize_seg: nseg must be in [1, 65535]");
+  if (out_dtype != MH3_DTYPE_E4M3 && out_dtype != MH3_DTYPE_F16)
+    return fail(MH3_ERR_INVALID, "mh3_quantize_seg: out_dtype must be e4m3 or f16");
+  if (head_block <= 0 || H % head_block || head_off < 0 || heads_sel <= 0 || head_off + heads_sel > head_block)
+    return fail(MH3_ERR_INVALID, "mh3_quantize_seg: bad head selection");
+  const quant::HeadSel sel{head_block, head_off, heads_sel};
+  if ((uintptr_t)out & 15u) return fail(MH3_ERR_INVALID, "mh3_quantize_seg: out must be 16-byte aligned");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const long long n = S * (H / head_block) * heads_sel * (D / 8);
+  const int blocks = (int)std::min<long long>((n + quant::kThreads - 1) / quant::kThreads, 148ll * 16);
+  const quant::Segs segs{seg, nseg};
+  uint8_t* o = static_cast<uint8_t*>(out);
+#define MH3_SEGQ(T, F16)                                                                                   \
+  quant::bh_quant_kernel<T, F16, true><<<blocks, quant::kThreads, 0, st>>>(static_cast<const T*>(x), 0, ss, sh, 1, \
+                                                                           (int)S, (int)H, (int)D, sel, segs, scale, o)
+  const bool f16 = out_dtype == MH3_DTYPE_F16;
+  if (in_dtype == MH3_DTYPE_BF16) {
+    if (f16) MH3_SEGQ(__nv_bfloat16, true); else MH3_SEGQ(__nv_bfloat16, false);
+  } else {
+    if (f16) MH3_SEGQ(__half, true); else MH3_SEGQ(__half, false);
+  }
+#undef MH3_SEGQ
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MH3_OK : fail_cuda(e, "mh3_quantize_seg launch");
 }
 
 extern "C" uint64_t mh3_qkv_workspace_bytes(int32_t batch, int32_t heads, int32_t seqlen_k, int32_t head_dim) {

@@ -26,6 +26,13 @@ exponential; this kernel already computes P from the exact exponential
 The op is registered as ``torch.ops.mh3.fp8_attention`` with a fake
 (meta) implementation, so ``torch.compile``d blocks trace through it
 without a graph break.
+
+``fp8_attention_varlen`` is this package's route for packed
+variable-length batches (video tokens followed by audio tokens per
+sample, ``cu_seqlens`` as in flash-attention's varlen interface), which the
+reference does not have: per-(sequence, head) absmax/448 scales for Q, K
+and V (``mh3_absmax_seg`` + ``mh3_quantize_seg``), then the same kernel
+over the packed tensors (op ``torch.ops.mh3.fp8_attention_varlen``).
 """
 from __future__ import annotations
 
@@ -128,3 +135,80 @@ def fp8_attention(
         raise ValueError("Unsupported inputs for fp8_attention")
     return torch.ops.mh3.fp8_attention(q, k, v, math.nan if scale is None else float(scale),
                                        key_mask, key_bias, float(repair_tau))
+
+
+def _check_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q):
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dim() != 3:
+            raise ValueError(f"{name} must be a CUDA tensor [tokens, heads, head_dim]")
+    if q.dtype not in (torch.bfloat16, torch.float16) or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("q, k, v must share one dtype, bf16 or f16")
+    if q.device != k.device or q.device != v.device:
+        raise ValueError("q, k, v must be on one device")
+    D = q.shape[2]
+    if D not in (64, 128) or k.shape[1:] != q.shape[1:] or v.shape != k.shape:
+        raise ValueError("q [Tq,H,D], k and v [Tk,H,D] with D 64 or 128")
+    for name, c in (("cu_seqlens_q", cu_seqlens_q), ("cu_seqlens_k", cu_seqlens_k)):
+        if not isinstance(c, torch.Tensor) or c.dtype != torch.int32 or c.dim() != 1 or c.device != q.device:
+            raise ValueError(f"{name} must be an int32 tensor [nseq+1] on q's device")
+    if cu_seqlens_q.numel() != cu_seqlens_k.numel() or cu_seqlens_q.numel() < 2:
+        raise ValueError("cu_seqlens_q and cu_seqlens_k must both hold nseq+1 >= 2 offsets")
+    if int(max_seqlen_q) <= 0:
+        raise ValueError("max_seqlen_q must be positive")
+    if not _device_is_sm100(q.device):
+        raise ValueError("fp8_attention_varlen needs an sm_100 device")
+
+
+def _per_segment_scales(x, cu):
+    return torch.clamp(_ops.absmax_seg(x, cu), min=1e-12) / 448.0          # [nseq, H]
+
+
+def _fp8_attention_varlen_impl(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, scale):
+    D = q.shape[2]
+    ls2 = (scale if scale is not None else 1.0 / math.sqrt(D)) * LOG2E
+    cq, ck = cu_seqlens_q.contiguous(), cu_seqlens_k.contiguous()
+    sq, sk, sv = _per_segment_scales(q, cq), _per_segment_scales(k, ck), _per_segment_scales(v, ck)
+    q8 = _ops.quantize_seg(q, cq, sq, torch.float8_e4m3fn)[0, 0]
+    k8 = _ops.quantize_seg(k, ck, sk, torch.float8_e4m3fn)[0, 0]
+    v8 = _ops.quantize_seg(v, ck, sv, _pv_dtype())[0, 0]
+    out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    return _ops.attention_e4m3(q8, k8, v8, sq[..., None], sk[..., None], sv[..., None], logit_scale_log2=ls2,
+                               out_dtype=q.dtype, cu_seqlens_q=cq, cu_seqlens_k=ck,
+                               max_seqlen_q=int(max_seqlen_q), out=out)
+
+
+@torch.library.custom_op("mh3::fp8_attention_varlen", mutates_args=())
+def _fp8_attention_varlen_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens_q: torch.Tensor,
+                             cu_seqlens_k: torch.Tensor, max_seqlen_q: int, scale: float) -> torch.Tensor:
+    return _fp8_attention_varlen_impl(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
+                                      None if math.isnan(scale) else scale)
+
+
+@_fp8_attention_varlen_op.register_fake
+def _(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, scale):
+    return torch.empty(q.shape, dtype=q.dtype, device=q.device)
+
+
+def fp8_attention_varlen(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    cu_seqlens_q: torch.Tensor,
+    cu_seqlens_k: torch.Tensor,
+    max_seqlen_q: int,
+    scale: float | None = None,
+) -> torch.Tensor:
+    """Non-causal FP8 attention over packed sequences.
+
+    q [Tq, H, D], k and v [Tk, H, D] (bf16 or f16, D 64 or 128); sequence i
+    is query rows ``[cu_seqlens_q[i], cu_seqlens_q[i+1])`` attending over key
+    rows ``[cu_seqlens_k[i], cu_seqlens_k[i+1])`` (int32 offsets on q's
+    device, non-decreasing); ``max_seqlen_q`` bounds the query lengths.
+    Quantisation is per (sequence, head): absmax/448 for Q, K and V (V as f16
+    V/scale for the f16 PV product unless ``MH3_PV_DTYPE=e4m3``).  Returns
+    [Tq, H, D] in q's dtype; rows outside every sequence are not written
+    (their values are unspecified).  ``scale`` defaults to 1/sqrt(D).
+    """
+    _check_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q)
+    return torch.ops.mh3.fp8_attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, int(max_seqlen_q),
+                                              math.nan if scale is None else float(scale))

@@ -396,6 +396,70 @@ def quantize_bh(x: torch.Tensor, scale: torch.Tensor, out_dtype: torch.dtype = E
     return out
 
 
+def _seg_args(x: torch.Tensor, seg: torch.Tensor):
+    """Packed x [S, H, D] or [1, S, H, D] and int32 segment bounds [nseg+1] on x's device."""
+    if x.dim() == 4:
+        if x.shape[0] != 1:
+            raise ValueError("a packed shard has batch 1: [1, S, H, D] or [S, H, D]")
+        x = x[0]
+    if not x.is_cuda or x.dim() != 3 or x.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("expected a CUDA bf16/f16 tensor [S, H, D]")
+    if x.stride(-1) != 1 or x.data_ptr() % 16 or any(st % 8 for st in x.stride()[:2]):
+        x = x.contiguous()
+    if not isinstance(seg, torch.Tensor) or seg.dtype != torch.int32 or seg.dim() != 1 or seg.numel() < 2:
+        raise ValueError("seg must be an int32 tensor [nseg+1]")
+    if seg.device != x.device:
+        raise ValueError("seg must be on x's device")
+    seg = seg.contiguous()
+    S, H, D = x.shape
+    return x, seg, (x.data_ptr(), _dtype_code(x.dtype), S, H, D, x.stride(0), x.stride(1))
+
+
+def absmax_seg(x: torch.Tensor, seg: torch.Tensor, groups: int = 1, head_off: int = 0,
+               heads_sel: int | None = None) -> torch.Tensor:
+    """max |x[rows of segment z, h, :]| as float32 [nseg, groups*heads_sel] for a packed shard
+    x [S, H, D] whose rows [seg[z], seg[z+1]) form segment z (entries clamped to [0, S];
+    ``mh3_absmax_seg``); heads selected as in ``absmax_bh``."""
+    lib = _lib.load()
+    x, seg, args = _seg_args(x, seg)
+    hb, off, hs = _head_sel(x.shape[1], groups, head_off, heads_sel)
+    nseg = seg.numel() - 1
+    out = torch.empty((nseg, groups * hs), dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        rc = lib.mh3_absmax_seg(*args, hb, off, hs, seg.data_ptr(), nseg, out.data_ptr(), _stream(x.device))
+    _lib.check(rc, "mh3_absmax_seg")
+    return out
+
+
+def quantize_seg(x: torch.Tensor, seg: torch.Tensor, scale: torch.Tensor, out_dtype: torch.dtype = E4M3,
+                 groups: int = 1, out: torch.Tensor | None = None, head_off: int = 0,
+                 heads_sel: int | None = None) -> torch.Tensor:
+    """Packed x [S, H, D] / scale[z, j] for the rows of segment z -> e4m3 (clamped to +-448) or
+    f16, as [groups, 1, S, heads_sel, D] (``mh3_quantize_seg``; rows outside every segment are
+    zeros; heads selected and numbered as in ``quantize_bh``)."""
+    lib = _lib.load()
+    x, seg, args = _seg_args(x, seg)
+    S, H, D = x.shape
+    if out_dtype not in (E4M3, torch.float16):
+        raise ValueError("out_dtype must be float8_e4m3fn or float16")
+    hb, off, hs = _head_sel(H, groups, head_off, heads_sel)
+    nseg = seg.numel() - 1
+    scale = scale.to(device=x.device, dtype=torch.float32).contiguous()
+    if scale.numel() != nseg * groups * hs:
+        raise ValueError("scale must hold one value per (segment, selected head)")
+    shape = (groups, 1, S, hs, D)
+    if out is None:
+        out = torch.empty(shape, dtype=out_dtype, device=x.device)
+    elif tuple(out.shape) != shape or out.dtype != out_dtype or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous {out_dtype} tensor of shape {shape}")
+    code = _lib.MH3_DTYPE_F16 if out_dtype == torch.float16 else _lib.MH3_DTYPE_E4M3
+    with torch.cuda.device(x.device):
+        rc = lib.mh3_quantize_seg(*args, hb, off, hs, seg.data_ptr(), nseg, scale.data_ptr(), code, out.data_ptr(),
+                                  _stream(x.device))
+    _lib.check(rc, "mh3_quantize_seg")
+    return out
+
+
 # ---------------------------------------------------------------------------
 # scaled GEMM / FP8 linear
 # ---------------------------------------------------------------------------

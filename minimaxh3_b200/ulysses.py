@@ -1,8 +1,8 @@
 """Ulysses (head-parallel) sharding of FP8 attention over NCCL.
 
 The reference runs one GPU per container and has no sequence or head
-parallelism; BASELINE config 5 asks for S=75600 self-attention sharded over
-2/4/8 GPUs.  Each rank holds a contiguous sequence shard of q, k, v
+parallelism; the long-sequence workload (S=75600 self-attention) is sharded
+here over 2/4/8 GPUs.  Each rank holds a contiguous sequence shard of q, k, v
 ``[B, S_local, H, D]`` (the layout a sequence-parallel DiT block holds).  Rank
 r attends over heads ``[r*H/P, (r+1)*H/P)``.  The heads are processed in
 ``head_groups`` groups G; group g takes local heads ``[g*Hg, (g+1)*Hg)``,
@@ -11,8 +11,8 @@ p.  Per group:
 
 1. per-(batch, head) absmax of the local shard's group heads
    (``mh3_absmax_bh`` with a head selection) and one ``all_reduce(MAX)``, so
-   every rank quantises with the global per-(b,h) scale (BASELINE configs
-   2/3/5 use per-(b,h) scales);
+   every rank quantises with the global per-(b,h) scale (the benchmark
+   workloads use per-(b,h) scales);
 2. local e4m3 quantisation (V: f16 V/scale for the f16 PV product, or e4m3)
    straight into the send layout ``[P, B, S_local, Hg, D]``
    (``mh3_quantize_bh``, one read of the bf16 group heads, no fp32
@@ -34,6 +34,17 @@ all-reduce, group g+1's quantisation + all-to-all and group g's attention +
 all-to-all back before it waits on anything of group g-1, so the exchanges of
 neighbouring groups overlap the attention kernel.  Every quantity is per
 (batch, head), so the result is the same, bit for bit, for every G.
+
+Packed variable-length batches (``cu_seqlens``: global token offsets of the
+sequences packed along S, batch 1) keep the offsets global: rank r's shard
+holds tokens ``[r*S_local, (r+1)*S_local)``, the scales are per (sequence,
+head) (``mh3_absmax_seg`` over the shard's part of each sequence, then the
+same ``all_reduce(MAX)``), the quantisation picks each row's sequence scale
+(``mh3_quantize_seg``; rows outside every sequence become zeros), and after
+the all-to-all the received ``[S, Hg, D]`` buffer is exactly the packed
+layout the varlen kernel reads with the global ``cu_seqlens``.  Output rows
+outside every sequence are zeros.  A packed total that is not a multiple of
+the world size is padded by the caller with tokens past the last sequence.
 
 ``ulysses_attention_host`` runs the same pipeline on shards in pinned host
 memory: each group's heads are copied in (one strided copy per tensor) on
@@ -76,6 +87,52 @@ def _cuda_quant(x, scale, P, out_dtype, head_off=0, heads_sel=None):
     return ops.quantize_bh(x, scale, out_dtype=out_dtype, groups=P, head_off=head_off, heads_sel=heads_sel)
 
 
+def _cuda_absmax_seg(x, groups=1, head_off=0, heads_sel=None, seg=None):
+    """[nseq, groups*heads_sel] per-(sequence, selected head) absmax of a packed shard: ``mh3_absmax_seg``."""
+    from . import ops
+
+    return ops.absmax_seg(x, seg, groups=groups, head_off=head_off, heads_sel=heads_sel)
+
+
+def _cuda_quant_seg(x, scale, P, out_dtype, head_off=0, heads_sel=None, seg=None):
+    """Packed [1,S_l,H,D] / scale[nseq, P*hs] -> [P, 1, S_l, hs, D], zeros outside every sequence:
+    ``mh3_quantize_seg``."""
+    from . import ops
+
+    return ops.quantize_seg(x, seg, scale, out_dtype=out_dtype, groups=P, head_off=head_off, heads_sel=heads_sel)
+
+
+class _Packing:
+    """Global ``cu_seqlens`` of a packed batch and this rank's view of them."""
+
+    _cache: dict = {}
+
+    def __init__(self, cu, P, r, S_l, device):
+        cu = [int(c) for c in (cu.tolist() if isinstance(cu, torch.Tensor) else cu)]
+        T = P * S_l
+        if len(cu) < 2 or any(b < a for a, b in zip(cu, cu[1:])) or cu[0] < 0 or cu[-1] > T:
+            raise ValueError(f"cu_seqlens must be non-decreasing offsets within [0, {T}] (P * S_local)")
+        self.nseq = len(cu) - 1
+        self.max_seqlen = max(max(b - a for a, b in zip(cu, cu[1:])), 1)
+        self.first, self.last = cu[0], cu[-1]
+        key = (tuple(cu), r, S_l, str(device))
+        tensors = _Packing._cache.get(key)
+        if tensors is None:
+            if len(_Packing._cache) >= 16:
+                _Packing._cache.pop(next(iter(_Packing._cache)))
+            local = [min(max(c - r * S_l, 0), S_l) for c in cu]
+            tensors = _Packing._cache[key] = (torch.tensor(cu, dtype=torch.int32, device=device),
+                                              torch.tensor(local, dtype=torch.int32, device=device))
+        self.cu, self.seg = tensors
+
+    def clear_outside(self, rows):
+        """Zero the rows of a [T, ...] tensor (global token order) outside every sequence."""
+        if self.first > 0:
+            rows[:self.first].zero_()
+        if self.last < rows.shape[0]:
+            rows[self.last:].zero_()
+
+
 def global_absmax(xs, group=None, absmax_fn=None):
     """[len(xs), B, H] float32 absmax over (S, D) of each [B,S_local,H,D], max-reduced over ranks."""
     fn = absmax_fn or _cuda_absmax
@@ -100,10 +157,13 @@ def _head_major(recv):
     return recv.permute(1, 3, 0, 2, 4).reshape(B, Hg, P * S_l, D)
 
 
-def _default_attn(q8, k8, v, sq, sk, sv, logit_scale_log2, out=None):
+def _default_attn(q8, k8, v, sq, sk, sv, logit_scale_log2, out=None, cu_seqlens=None, max_seqlen=0):
     from . import ops
 
-    return ops.attention_e4m3(q8, k8, v, sq, sk, sv, logit_scale_log2=logit_scale_log2, out=out)
+    kw = {} if out is None else {"out": out, "out_dtype": out.dtype}
+    if cu_seqlens is not None:
+        kw.update(cu_seqlens_q=cu_seqlens, cu_seqlens_k=cu_seqlens, max_seqlen_q=max_seqlen)
+    return ops.attention_e4m3(q8, k8, v, sq, sk, sv, logit_scale_log2=logit_scale_log2, **kw)
 
 
 def default_head_groups(local_heads: int) -> int:
@@ -139,27 +199,32 @@ class _Pipeline:
     the compute stream.
     """
 
-    def __init__(self, P, r, Hg, shape, out_dtype, group, pv_dtype, ls2, attn_fn, absmax_fn, quant_fn, events):
+    def __init__(self, P, r, Hg, shape, out_dtype, group, pv_dtype, ls2, attn_fn, absmax_fn, quant_fn, events,
+                 packing=None):
         self.P, self.r, self.Hg = P, r, Hg
         self.B, self.S_l, self.D = shape
         self.out_dtype, self.group, self.pv_dtype, self.ls2 = out_dtype, group, pv_dtype, ls2
         self.attn = attn_fn or _default_attn
         self.direct = attn_fn is None and self.B == 1
-        self.absmax_fn = absmax_fn or _cuda_absmax
-        self.quant_fn = quant_fn or _cuda_quant
+        self.packing = packing
+        # packed batches: the scale axis is the sequence, the kernels get the shard's segment bounds
+        self.seg_kw = {} if packing is None else {"seg": packing.seg}
+        self.absmax_fn = absmax_fn or (_cuda_absmax if packing is None else _cuda_absmax_seg)
+        self.quant_fn = quant_fn or (_cuda_quant if packing is None else _cuda_quant_seg)
         self.events = events
 
     def absmax(self, xs, off):
-        local = torch.stack([self.absmax_fn(x, groups=self.P, head_off=off, heads_sel=self.Hg) for x in xs])
+        local = torch.stack([self.absmax_fn(x, groups=self.P, head_off=off, heads_sel=self.Hg, **self.seg_kw)
+                             for x in xs])
         work = dist.all_reduce(local, op=dist.ReduceOp.MAX, group=self.group, async_op=True)
         return local, work
 
     def exchange_in(self, xs, off, amax, work):
         work.wait()
-        scales = torch.clamp(amax, min=1e-12) / 448.0          # [3, B, P*Hg]
+        scales = torch.clamp(amax, min=1e-12) / 448.0          # [3, B (packed: nseq), P*Hg]
         recvs, works = [], []
         for x, s, dt in zip(xs, scales, (E4M3, E4M3, self.pv_dtype)):
-            send = self.quant_fn(x, s, self.P, dt, head_off=off, heads_sel=self.Hg)
+            send = self.quant_fn(x, s, self.P, dt, head_off=off, heads_sel=self.Hg, **self.seg_kw)
             recv, w = _exchange_async(send, self.group)
             recvs.append(recv)
             works.append((w, send))                             # send stays alive until the wait
@@ -170,24 +235,37 @@ class _Pipeline:
             w.wait()
         P, B, S_l, Hg, D = self.P, self.B, self.S_l, self.Hg, self.D
         mine = slice(self.r * Hg, (self.r + 1) * Hg)
-        sq, sk, sv = (s[:, mine].contiguous()[..., None] for s in scales)  # [B, Hg, 1] per-(b,h)
-        hq, hk, hv = (_head_major(t) for t in recvs)
+        sq, sk, sv = (s[:, mine].contiguous()[..., None] for s in scales)  # [B or nseq, Hg, 1]
         send_o = torch.empty((P, B, S_l, Hg, D), dtype=self.out_dtype, device=recvs[0].device)
         ev = None
         if self.events is not None:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             ev[0].record()
-        if self.direct:
-            # token s of group head h sits at s*Hg*D + h*D of the send buffer
-            self.attn(hq, hk, hv, sq, sk, sv, self.ls2, out=send_o.view(P * S_l, Hg, D).permute(1, 0, 2).unsqueeze(0))
+        if self.packing is not None:
+            # B = 1: the received [P, 1, S_l, Hg, D] is the packed [S, Hg, D] in global token order
+            pk = self.packing
+            hq, hk, hv = (t.view(P * S_l, Hg, D) for t in recvs)
+            o_rows = send_o.view(P * S_l, Hg, D)
+            kw = {"cu_seqlens": pk.cu, "max_seqlen": pk.max_seqlen}
+            if self.direct:
+                self.attn(hq, hk, hv, sq, sk, sv, self.ls2, out=o_rows, **kw)
+            else:
+                o_rows.copy_(self.attn(hq, hk, hv, sq, sk, sv, self.ls2, **kw).to(self.out_dtype))
+            pk.clear_outside(o_rows)                           # the kernel writes no row outside a sequence
         else:
-            o = self.attn(hq, hk, hv, sq, sk, sv, self.ls2)     # [B, Hg, S, D]
+            hq, hk, hv = (_head_major(t) for t in recvs)
+            if self.direct:
+                # token s of group head h sits at s*Hg*D + h*D of the send buffer
+                self.attn(hq, hk, hv, sq, sk, sv, self.ls2,
+                          out=send_o.view(P * S_l, Hg, D).permute(1, 0, 2).unsqueeze(0))
+            else:
+                o = self.attn(hq, hk, hv, sq, sk, sv, self.ls2)     # [B, Hg, S, D]
+                # chunk p = tokens of rank p -> [P, B, S_l, Hg, D]
+                send_o.copy_(o.to(self.out_dtype).permute(2, 0, 1, 3).reshape(P, S_l, B, Hg, D)
+                             .permute(0, 2, 1, 3, 4))
         if ev is not None:
             ev[1].record()
             self.events.append(ev)
-        if not self.direct:
-            # chunk p = tokens of rank p -> [P, B, S_l, Hg, D]
-            send_o.copy_(o.to(self.out_dtype).permute(2, 0, 1, 3).reshape(P, S_l, B, Hg, D).permute(0, 2, 1, 3, 4))
         recv_o, w = _exchange_async(send_o, self.group)
         return recv_o, (w, send_o)
 
@@ -227,22 +305,36 @@ class _Pipeline:
         stage_d(G - 1)
 
 
+def _packing(cu_seqlens, P, r, B, S_l, device):
+    if cu_seqlens is None:
+        return None
+    if B != 1:
+        raise ValueError("cu_seqlens needs a packed batch: shards [1, S_local, H, D]")
+    return _Packing(cu_seqlens, P, r, S_l, device)
+
+
 def ulysses_attention(q, k, v, group=None, scale=None, pv_dtype=torch.float16, attn_fn=None, events=None,
-                      absmax_fn=None, quant_fn=None, head_groups=1, out=None):
+                      absmax_fn=None, quant_fn=None, head_groups=1, out=None, cu_seqlens=None):
     """Head-parallel FP8 attention of sequence shards ``[B, S_local, H, D]``.
 
     Returns the local output shard ``[B, S_local, H, D]`` (q's dtype; written
     into ``out`` when given, contiguous).  H must be divisible by the world
     size P and H/P by ``head_groups``; every rank must hold the same S_local.
+    ``cu_seqlens``: global offsets (host ints: a list or a CPU tensor, the same
+    on every rank) of sequences packed along S of a batch-1 input; attention
+    then stays inside each sequence, with per-(sequence, head) scales.
     ``events``: optional list that receives one (start, end) pair of timing
     CUDA events around each local attention launch.  ``attn_fn`` /
     ``absmax_fn`` / ``quant_fn`` replace the CUDA kernels (for CPU process
     groups in tests; absmax_fn / quant_fn take the head selection of
-    ``ops.absmax_bh`` / ``ops.quantize_bh``).
+    ``ops.absmax_bh`` / ``ops.quantize_bh``, plus ``seg=`` (the shard's
+    segment bounds) and attn_fn ``cu_seqlens=`` / ``max_seqlen=`` for a packed
+    batch).
     """
     P, r = _world(group)
     B, S_l, H, D = q.shape
     _check_heads(H, P, head_groups)
+    packing = _packing(cu_seqlens, P, r, B, S_l, q.device)
     Hl = H // P
     Hg = Hl // head_groups
     if out is None:
@@ -259,7 +351,8 @@ def ulysses_attention(q, k, v, group=None, scale=None, pv_dtype=torch.float16, a
         work.wait()
         oview[:, :, :, g * Hg:(g + 1) * Hg].copy_(recv_o.permute(1, 2, 0, 3, 4))
 
-    pipe = _Pipeline(P, r, Hg, (B, S_l, D), q.dtype, group, pv_dtype, ls2, attn_fn, absmax_fn, quant_fn, events)
+    pipe = _Pipeline(P, r, Hg, (B, S_l, D), q.dtype, group, pv_dtype, ls2, attn_fn, absmax_fn, quant_fn, events,
+                     packing)
     pipe.run(head_groups, source, sink)
     return out
 
@@ -282,7 +375,7 @@ class _HostShardBuffers:
 
 
 def ulysses_attention_host(q, k, v, out=None, group=None, scale=None, pv_dtype=torch.float16, head_groups=None,
-                           cross_kv=None, cross_out=None, events=None):
+                           cross_kv=None, cross_out=None, events=None, cu_seqlens=None):
     """``ulysses_attention`` of host-resident shards, streamed per head group.
 
     q, k, v: contiguous pinned CPU tensors ``[B, S_local, H, D]`` (bf16 or
@@ -297,7 +390,8 @@ def ulysses_attention_host(q, k, v, out=None, group=None, scale=None, pv_dtype=t
     replicated on every rank; then each group also runs ``fp8_attention`` of
     its query heads against them, written to ``cross_out`` (pinned CPU
     ``[B, S_local, H, D]``, allocated when None).  Returns ``out`` or
-    ``(out, cross_out)``.
+    ``(out, cross_out)``.  ``cu_seqlens``: as in ``ulysses_attention`` (not
+    with ``cross_kv``: each packed sequence would need its own text K/V).
     """
     from . import ops
 
@@ -308,10 +402,13 @@ def ulysses_attention_host(q, k, v, out=None, group=None, scale=None, pv_dtype=t
     B, S_l, H, D = q.shape
     G = head_groups or default_head_groups(H // P if H % P == 0 else 1)
     _check_heads(H, P, G)
+    if cu_seqlens is not None and cross_kv is not None:
+        raise ValueError("cross_kv is not supported with cu_seqlens")
     Hl = H // P
     Hg = Hl // G
     es = q.element_size()
     dev = torch.device("cuda", torch.cuda.current_device())
+    packing = _packing(cu_seqlens, P, r, B, S_l, dev)
 
     def host_like(t, name):
         if t is None:
@@ -380,7 +477,7 @@ def ulysses_attention_host(q, k, v, out=None, group=None, scale=None, pv_dtype=t
         ev.record(s_cmp)
         free[g] = ev
 
-    pipe = _Pipeline(P, r, Hg, (B, S_l, D), q.dtype, group, pv_dtype, ls2, None, None, None, events)
+    pipe = _Pipeline(P, r, Hg, (B, S_l, D), q.dtype, group, pv_dtype, ls2, None, None, None, events, packing)
     pipe.run(G, source, sink, on_quantized=quantized)
     s_cmp.wait_stream(s_out)
     return out if cross_kv is None else (out, cross_out)

@@ -21,7 +21,7 @@ def cpu_sdpa_fallback(query, key, value, attn_mask=None, dropout_p=0.0, is_causa
 
 
 def fp8_emulated_inputs(q, k, v):
-    """BASELINE config 1 variant: per-(b,h) absmax/448 e4m3 quantise-dequantise."""
+    """Benchmark configuration 1 variant: per-(b,h) absmax/448 e4m3 quantise-dequantise."""
     outs = []
     for x in (q, k, v):
         xf = x.float()

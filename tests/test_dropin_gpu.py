@@ -99,3 +99,62 @@ def test_is_supported_rules():
         from minimaxh3_b200.kernels.fp8_attention import fp8_attention
 
         fp8_attention(t.float(), t, t)
+
+
+@pytest.mark.parametrize("lens_q,lens_k,D,dtype", [
+    ([300, 0, 77, 513], None, 128, torch.bfloat16),      # an empty sequence, tails
+    ([200, 129], [640, 1], 128, torch.bfloat16),        # query and key packings differ; one key
+    ([1, 255, 384], None, 64, torch.float16),
+])
+def test_fp8_attention_varlen(lens_q, lens_k, D, dtype, record_margin):
+    """Packed sequences: per-(sequence, head) absmax/448 quantisation (V as f16 V/scale), attention
+    inside each sequence; every row against exact attention of those operands."""
+    from minimaxh3_b200.kernels.fp8_attention import fp8_attention_varlen
+
+    lens_k = lens_k or lens_q
+    H = 4
+    cu_q = torch.tensor([0] + list(torch.tensor(lens_q).cumsum(0)), dtype=torch.int32)
+    cu_k = torch.tensor([0] + list(torch.tensor(lens_k).cumsum(0)), dtype=torch.int32)
+    g = torch.Generator().manual_seed(sum(lens_q) + D)
+
+    def packed(T):
+        x = torch.randn(T, H, D, generator=g)
+        x[..., 9] *= 8.0
+        return x.to(dtype)
+
+    q, k, v = packed(int(cu_q[-1])), packed(int(cu_k[-1])), packed(int(cu_k[-1]))
+    out = fp8_attention_varlen(q.to(DEV), k.to(DEV), v.to(DEV), cu_q.to(DEV), cu_k.to(DEV), max(lens_q))
+    assert out.shape == q.shape and out.dtype == dtype
+    out = out.float().cpu()
+    ls2 = OA.LOG2E / math.sqrt(D)
+
+    def operand(x, dt):
+        s = torch.clamp(x.float().abs().amax(dim=(0, 2)), min=1e-12) / 448.0     # [H]
+        y = x.float() / s[None, :, None]
+        y = (torch.clamp(y, -448, 448) if dt == torch.float8_e4m3fn else y).to(dt)
+        return (y.double() * s.double()[None, :, None]).permute(1, 0, 2)[None]  # [1, H, L, D]
+
+    for z in range(len(lens_q)):
+        (a, b), (c, d) = (int(cu_q[z]), int(cu_q[z + 1])), (int(cu_k[z]), int(cu_k[z + 1]))
+        if b == a:
+            continue
+        ref = OA.sdpa_dequant_oracle(operand(q[a:b], torch.float8_e4m3fn), operand(k[c:d], torch.float8_e4m3fn),
+                                     operand(v[c:d], torch.float16), ls2, base2=True)[0].permute(1, 0, 2)
+        r = OA.compare(out[a:b], ref)
+        record_margin(r, f"varlen seq{z}")
+        assert OA.within_tolerance(r), (z, r)
+
+
+def test_fp8_attention_varlen_rejects_bad_arguments():
+    from minimaxh3_b200.kernels.fp8_attention import fp8_attention_varlen
+
+    x = torch.zeros(64, 2, 128, dtype=torch.bfloat16, device=DEV)
+    cu = torch.tensor([0, 64], dtype=torch.int32, device=DEV)
+    with pytest.raises(ValueError):
+        fp8_attention_varlen(x[None], x, x, cu, cu, 64)                 # not packed
+    with pytest.raises(ValueError):
+        fp8_attention_varlen(x, x, x, cu.long(), cu, 64)                # int32 offsets
+    with pytest.raises(ValueError):
+        fp8_attention_varlen(x, x, x, cu, torch.tensor([0, 32, 64], dtype=torch.int32, device=DEV), 64)
+    with pytest.raises(ValueError):
+        fp8_attention_varlen(x, x, x, cu, cu, 0)

@@ -2,7 +2,7 @@
 
 ``exp2_attention_emulation`` runs the CUDA kernel's block algorithm (lazy
 max threshold 4.5, P = f16 or e4m3 of 2^(t - m + 4),
-per 128-key tile) with exact exp2.  On the BASELINE value distribution (N(0,1) with 1% of channels x8)
+per 128-key tile) with exact exp2.  On the benchmark value distribution (N(0,1) with 1% of channels x8)
 it must meet cos >= 0.9995 and max-abs <= 2e-2 relative against float64
 softmax attention on the same dequantised inputs; the reference's bit-trick
 algorithm is shown alongside for the record.

@@ -1,9 +1,11 @@
-"""GPU parity at the BASELINE configurations' own sizes (through the C ABI).
+"""GPU parity at the benchmark configurations' own sizes (through the C ABI).
 
 * Config 3: packed joint video+audio attention, cu_seqlens [0, 33784, 50676]
   (32760+1024 and 16380+512 tokens), H=40, D=128, per-(sequence, head)
   e4m3 scales, f16 PV product.  Checked on sampled query rows of both
   sequences against exact softmax attention over that sequence's keys only.
+  The same lengths through the drop-in ``fp8_attention_varlen`` (bf16 in,
+  its own per-(sequence, head) quantisation).
 * Config 4: the FP8 scaled GEMM at M=32760, K=5120, N in {5120, 15360,
   13824} and the MLP-down shape (K=13824, N=5120): bit-equal to
   ``torch._scaled_mm`` with row-wise scales and bias (the reference's call,
@@ -42,7 +44,7 @@ def test_config3_packed_varlen_attention(record_margin):
     g = torch.Generator(device=DEV).manual_seed(3)
     gc = torch.Generator().manual_seed(3)
     xs = [_outlier_randn(g, (T, H, D), D, gc) for _ in range(3)]
-    # per-(sequence, head) absmax scales, e4m3
+    # per-(sequence, head) absmax scales, e4m3 (benchmark configuration 3)
     q8s, scales = [], []
     for x in xs:
         s = torch.empty(len(lens), H, 1, device=DEV)
@@ -73,6 +75,52 @@ def test_config3_packed_varlen_attention(record_margin):
             got = out[lo:hi, h][rows.to(DEV)].float().cpu()
             r = OA.compare(got, ref)
             record_margin(r, f"seq{b} head{h}")
+            assert OA.within_tolerance(r), (b, h, r)
+
+
+def test_config3_through_the_varlen_dropin(record_margin):
+    """``fp8_attention_varlen`` on bf16 packed q/k/v at config 3's lengths: its per-(sequence, head)
+    quantisation gives the kernel exactly the operands of a torch restatement (outputs bit-equal),
+    and sampled rows are within tolerance of exact attention on those operands."""
+    from minimaxh3_b200 import ops
+    from minimaxh3_b200.kernels.fp8_attention import fp8_attention_varlen
+
+    H, D = 40, 128
+    lens = [33784, 16892]
+    cu = torch.tensor([0, lens[0], lens[0] + lens[1]], dtype=torch.int32, device=DEV)
+    T = lens[0] + lens[1]
+    g = torch.Generator(device=DEV).manual_seed(31)
+    gc = torch.Generator().manual_seed(31)
+    q, k, v = (_outlier_randn(g, (T, H, D), D, gc).to(torch.bfloat16) for _ in range(3))
+    out = fp8_attention_varlen(q, k, v, cu, cu, max(lens))
+    ops_in, scales = [], []
+    for x, dt in ((q, torch.float8_e4m3fn), (k, torch.float8_e4m3fn), (v, torch.float16)):
+        s = torch.empty(len(lens), H, 1, device=DEV)
+        y = torch.empty(T, H, D, dtype=dt, device=DEV)
+        for b in range(len(lens)):
+            lo, hi = int(cu[b]), int(cu[b + 1])
+            s[b, :, 0] = torch.clamp(x[lo:hi].float().abs().amax(dim=(0, 2)), min=1e-12) / 448.0
+            t = x[lo:hi].float() / s[b, :, 0][None, :, None]
+            y[lo:hi] = (torch.clamp(t, -448, 448) if dt == torch.float8_e4m3fn else t).to(dt)
+        ops_in.append(y)
+        scales.append(s)
+    del q, k, v
+    ls2 = OA.LOG2E / math.sqrt(D)
+    ref_kernel = ops.attention_e4m3(*ops_in, *scales, logit_scale_log2=ls2, cu_seqlens_q=cu, cu_seqlens_k=cu,
+                                    max_seqlen_q=max(lens))
+    assert torch.equal(out, ref_kernel)
+    (q8, k8, v16), (sq, sk, sv) = ops_in, scales
+    gs = torch.Generator().manual_seed(34)
+    for b in range(len(lens)):
+        lo, hi = int(cu[b]), int(cu[b + 1])
+        rows = torch.cat([torch.tensor([0, hi - lo - 1]), torch.randint(1, hi - lo - 1, (16,), generator=gs)])
+        for h in (3, 38):
+            qd = q8[lo:hi, h][rows].double().cpu() * float(sq[b, h, 0])
+            kd = k8[lo:hi, h].double().cpu() * float(sk[b, h, 0])
+            vd = v16[lo:hi, h].double().cpu() * float(sv[b, h, 0])
+            ref = OA.sdpa_dequant_oracle(qd[None, None], kd[None, None], vd[None, None], ls2, base2=True)[0, 0]
+            r = OA.compare(out[lo:hi, h][rows.to(DEV)].float().cpu(), ref)
+            record_margin(r, f"drop-in seq{b} head{h}")
             assert OA.within_tolerance(r), (b, h, r)
 
 

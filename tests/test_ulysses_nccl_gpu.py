@@ -1,5 +1,6 @@
 """Ulysses over NCCL on 2 GPUs: bit-identical to one GPU over the whole sequence,
-for every head grouping of the pipeline and for the host-resident variant.
+for every head grouping of the pipeline, for the host-resident variant and
+for sequences packed with global cu_seqlens (against the drop-in varlen path).
 
 Every rank quantises with the global per-(batch, head) scales, so the head
 shard each rank attends over holds exactly the bytes a single GPU would use;
@@ -33,6 +34,21 @@ def _inputs(B, S, H, D):
     return xs
 
 
+# sequences packed along S (global offsets): one crosses the rank boundary, the last 40 rows lie outside
+PACKED_CU = [0, 1000, 2900, 3800]
+
+
+def _packed_single_gpu(q, k, v, cu):
+    """The drop-in varlen path on one GPU over the whole packed sequence; rows outside every sequence zeroed."""
+    from minimaxh3_b200.kernels.fp8_attention import fp8_attention_varlen
+
+    cut = torch.tensor(cu, dtype=torch.int32, device=q.device)
+    o = fp8_attention_varlen(q[0], k[0], v[0], cut, cut, max(b - a for a, b in zip(cu, cu[1:])))
+    o[:cu[0]] = 0
+    o[cu[-1]:] = 0
+    return o[None]
+
+
 def _worker(rank, world, port, shape, out_dir):
     import datetime
 
@@ -52,6 +68,7 @@ def _worker(rank, world, port, shape, out_dir):
         sl = slice(rank * Sl, (rank + 1) * Sl)
         shard = [t[:, sl].contiguous() for t in (q, k, v)]
         outs = {G: ulysses_attention(*shard, head_groups=G) for G in (1, 2, 4)}
+        packed = {G: ulysses_attention(*shard, head_groups=G, cu_seqlens=PACKED_CU) for G in (1, 2)}
         # host-resident shards, with the cross-attention to replicated text K/V per head group
         gt = torch.Generator().manual_seed(11)
         kt, vt = (torch.randn(B, H, 256, D, generator=gt).to(torch.bfloat16).cuda() for _ in range(2))
@@ -59,8 +76,11 @@ def _worker(rank, world, port, shape, out_dir):
         ho, hc = ulysses_attention_host(hq, hk, hv, head_groups=2, cross_kv=(kt, vt))
         cross = fp8_attention(shard[0].transpose(1, 2), kt, vt).transpose(1, 2)
         torch.cuda.synchronize()
+        hp = ulysses_attention_host(hq, hk, hv, head_groups=2, cu_seqlens=PACKED_CU)
+        torch.cuda.synchronize()
         torch.save({"out": {G: o.cpu() for G, o in outs.items()}, "host": ho.clone(), "host_cross": hc.clone(),
-                    "cross": cross.cpu()}, os.path.join(out_dir, f"out{rank}.pt"))
+                    "cross": cross.cpu(), "packed": {G: o.cpu() for G, o in packed.items()},
+                    "host_packed": hp.clone()}, os.path.join(out_dir, f"out{rank}.pt"))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -100,6 +120,11 @@ def test_ulysses_two_gpus_bit_identical(tmp_path):
     ref = ops.attention_e4m3(*ops_in, *scales, logit_scale_log2=1.4426950408889634 / math.sqrt(D))
     ref = ref.permute(0, 2, 1, 3).cpu()
     assert torch.equal(got, ref)
+    # packed sequences: global cu_seqlens, per-(sequence, head) scales reduced over the ranks
+    packed_ref = _packed_single_gpu(q, k, v, PACKED_CU).cpu()
+    for G in (1, 2):
+        assert torch.equal(torch.cat([x["packed"][G] for x in res], dim=1), packed_ref)
+    assert torch.equal(torch.cat([x["host_packed"] for x in res], dim=1), packed_ref)
 
 
 def _single_rank_worker(port, out_dir):
@@ -127,14 +152,21 @@ def _single_rank_worker(port, out_dir):
             o, c = ulysses_attention_host(hq, hk, hv, head_groups=G, cross_kv=(kt, vt))
             torch.cuda.synchronize()
             res.append((o.clone(), c.clone()))
-        torch.save({"dev": dev_out.cpu(), "cross": cross.cpu(), "host": res}, os.path.join(out_dir, "single.pt"))
+        cu = [0, 400, 400, 900]                  # an empty sequence; rows 900.. outside every sequence
+        packed = ulysses_attention(q, k, v, cu_seqlens=cu)
+        packed_host = ulysses_attention_host(hq, hk, hv, head_groups=2, cu_seqlens=torch.tensor(cu))
+        torch.cuda.synchronize()
+        torch.save({"dev": dev_out.cpu(), "cross": cross.cpu(), "host": res, "packed": packed.cpu(),
+                    "packed_host": packed_host.clone(), "packed_ref": _packed_single_gpu(q, k, v, cu).cpu()},
+                   os.path.join(out_dir, "single.pt"))
     finally:
         dist.destroy_process_group()
 
 
 def test_host_resident_pipeline_on_one_rank(tmp_path):
     """ulysses_attention_host on a one-rank NCCL group equals the device path and per-group
-    cross-attention bit for bit, also when a call reuses the previous call's device buffers."""
+    cross-attention bit for bit, also when a call reuses the previous call's device buffers;
+    with cu_seqlens both equal ``fp8_attention_varlen``."""
     ctx = mp.get_context("spawn")
     p = ctx.Process(target=_single_rank_worker, args=(_free_port(), str(tmp_path)))
     p.start()
@@ -144,3 +176,6 @@ def test_host_resident_pipeline_on_one_rank(tmp_path):
     for o, c in r["host"]:
         assert torch.equal(o, r["dev"])
         assert torch.equal(c, r["cross"])
+    assert torch.equal(r["packed"], r["packed_ref"])          # Ulysses with cu_seqlens = the drop-in varlen path
+    assert torch.equal(r["packed_host"], r["packed_ref"])
+    assert torch.count_nonzero(r["packed"][0, 900:]) == 0
