@@ -366,7 +366,7 @@ def config5_single_gpu(dev, steps=3, warmup=1):
 
     def step():
         amax = torch.stack([ops.absmax_bh(t) for t in (q, k, v)])        # [3, B, H]
-        sc = torch.clamp(amax, min=1e-12) / 448.0
+        sc = ops.scale_from_absmax(amax)
         q8 = ops.quantize_bh(q, sc[0])[0].transpose(1, 2)                 # [B, H, S, D] views
         k8 = ops.quantize_bh(k, sc[1])[0].transpose(1, 2)
         v16 = ops.quantize_bh(v, sc[2], out_dtype=torch.float16)[0].transpose(1, 2)

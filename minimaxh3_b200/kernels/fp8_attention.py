@@ -160,7 +160,7 @@ def _check_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q):
 
 
 def _per_segment_scales(x, cu):
-    return torch.clamp(_ops.absmax_seg(x, cu), min=1e-12) / 448.0          # [nseq, H]
+    return _ops.scale_from_absmax(_ops.absmax_seg(x, cu))                  # [nseq, H]
 
 
 def _fp8_attention_varlen_impl(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, scale):

@@ -396,6 +396,20 @@ def quantize_bh(x: torch.Tensor, scale: torch.Tensor, out_dtype: torch.dtype = E
     return out
 
 
+def scale_from_absmax(amax: torch.Tensor) -> torch.Tensor:
+    """Per-(batch or sequence, head) e4m3 scale ``max(amax, 1e-12) / 448`` as float32, rounded
+    correctly (the IEEE quotient, as the library's own kernels compute it) on any device.
+
+    ``tensor / 448.0`` would not do on CUDA: torch multiplies by the rounded reciprocal of a
+    Python-scalar divisor, which misses the quotient by one ulp for some values, and a scale one
+    ulp off moves elements across e4m3 rounding boundaries.  The quotient is taken in float64 and
+    rounded once to float32; for the divisor 448 = 7 * 2^6 that is always the correctly rounded
+    float32 quotient (a float32 divided by 7 is never within a float64 error of a float32
+    rounding midpoint)."""
+    a = torch.clamp(amax.to(torch.float32), min=1e-12)
+    return (a.to(torch.float64) / 448.0).to(torch.float32)
+
+
 def _seg_args(x: torch.Tensor, seg: torch.Tensor):
     """Packed x [S, H, D] or [1, S, H, D] and int32 segment bounds [nseg+1] on x's device."""
     if x.dim() == 4:

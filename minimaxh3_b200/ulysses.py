@@ -133,6 +133,12 @@ class _Packing:
             rows[self.last:].zero_()
 
 
+def _scale_from_absmax(amax):
+    from . import ops
+
+    return ops.scale_from_absmax(amax)
+
+
 def global_absmax(xs, group=None, absmax_fn=None):
     """[len(xs), B, H] float32 absmax over (S, D) of each [B,S_local,H,D], max-reduced over ranks."""
     fn = absmax_fn or _cuda_absmax
@@ -221,7 +227,7 @@ class _Pipeline:
 
     def exchange_in(self, xs, off, amax, work):
         work.wait()
-        scales = torch.clamp(amax, min=1e-12) / 448.0          # [3, B (packed: nseq), P*Hg]
+        scales = _scale_from_absmax(amax)                      # [3, B (packed: nseq), P*Hg]
         recvs, works = [], []
         for x, s, dt in zip(xs, scales, (E4M3, E4M3, self.pv_dtype)):
             send = self.quant_fn(x, s, self.P, dt, head_off=off, heads_sel=self.Hg, **self.seg_kw)

@@ -130,3 +130,17 @@ def test_segment_kernels_reject_bad_arguments():
         ops.quantize_seg(x, seg, torch.ones(2, 4, device="cuda"))        # one scale row per segment
     with pytest.raises(ValueError):
         ops.absmax_seg(torch.zeros(2, 64, 4, 128, dtype=torch.bfloat16, device="cuda"), seg)   # batch 2
+
+
+def test_scale_from_absmax_on_the_device_is_correctly_rounded():
+    """The scale helper the varlen and Ulysses paths use gives the IEEE float32 quotient on CUDA
+    tensors too (the same bits as the quantisation kernels' own division)."""
+    import numpy as np
+
+    from minimaxh3_b200 import ops
+
+    g = torch.Generator().manual_seed(1)
+    amax = torch.cat([torch.rand(200000, generator=g) * 40, torch.exp(torch.randn(200000, generator=g) * 20)]).float()
+    got = ops.scale_from_absmax(amax.cuda()).cpu()
+    ref = np.maximum(amax.numpy(), np.float32(1e-12)) / np.float32(448.0)
+    assert np.array_equal(got.numpy(), ref)

@@ -129,7 +129,7 @@ def test_fp8_attention_varlen(lens_q, lens_k, D, dtype, record_margin):
     ls2 = OA.LOG2E / math.sqrt(D)
 
     def operand(x, dt):
-        s = torch.clamp(x.float().abs().amax(dim=(0, 2)), min=1e-12) / 448.0     # [H]
+        s = (torch.clamp(x.float().abs().amax(dim=(0, 2)), min=1e-12).double() / 448.0).float()     # [H]
         y = x.float() / s[None, :, None]
         y = (torch.clamp(y, -448, 448) if dt == torch.float8_e4m3fn else y).to(dt)
         return (y.double() * s.double()[None, :, None]).permute(1, 0, 2)[None]  # [1, H, L, D]

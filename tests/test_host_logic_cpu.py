@@ -37,3 +37,20 @@ def test_head_groups_defaults_and_checks():
         _check_heads(40, 3, 1)
     with pytest.raises(ValueError):
         _check_heads(40, 2, 3)
+
+
+def test_scale_from_absmax_is_the_correctly_rounded_quotient():
+    """max(amax, 1e-12) / 448 in float32, rounded once - the IEEE quotient the quantisation
+    kernels compute, whatever the device's scalar-division shortcut."""
+    import numpy as np
+    import torch
+
+    from minimaxh3_b200 import ops
+
+    g = torch.Generator().manual_seed(0)
+    amax = torch.cat([torch.rand(100000, generator=g) * 40, torch.exp(torch.randn(100000, generator=g) * 20),
+                      torch.tensor([0.0, 1e-13, 448.0, 3.4e38, 1.0])]).float()
+    got = ops.scale_from_absmax(amax)
+    ref = np.maximum(amax.numpy(), np.float32(1e-12)) / np.float32(448.0)   # numpy float32: IEEE division
+    assert got.dtype == torch.float32
+    assert np.array_equal(got.numpy(), ref)

@@ -99,7 +99,8 @@ def test_config3_through_the_varlen_dropin(record_margin):
         y = torch.empty(T, H, D, dtype=dt, device=DEV)
         for b in range(len(lens)):
             lo, hi = int(cu[b]), int(cu[b + 1])
-            s[b, :, 0] = torch.clamp(x[lo:hi].float().abs().amax(dim=(0, 2)), min=1e-12) / 448.0
+            # the correctly rounded quotient (float64, rounded once), as the drop-in computes it
+            s[b, :, 0] = (torch.clamp(x[lo:hi].float().abs().amax(dim=(0, 2)), min=1e-12).double() / 448.0).float()
             t = x[lo:hi].float() / s[b, :, 0][None, :, None]
             y[lo:hi] = (torch.clamp(t, -448, 448) if dt == torch.float8_e4m3fn else t).to(dt)
         ops_in.append(y)

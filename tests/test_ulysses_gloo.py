@@ -82,7 +82,7 @@ def _reference(B, S, H, D, pv):
     outs = []
     scales = []
     for x, dt in ((q, torch.float8_e4m3fn), (k, torch.float8_e4m3fn), (v, pv)):
-        s = torch.clamp(x.float().abs().amax(dim=(1, 3)), min=1e-12) / 448.0   # [B,H]
+        s = (torch.clamp(x.float().abs().amax(dim=(1, 3)), min=1e-12).double() / 448.0).float()   # [B,H]
         y = x.float() / s[:, None, :, None]
         if dt == torch.float8_e4m3fn:
             y = torch.clamp(y, -448, 448)
@@ -211,7 +211,7 @@ def _packed_reference(S, H, D, cu, pv):
     seg = torch.tensor(cu, dtype=torch.int32)
     ops_in, scales = [], []
     for x, dt in ((q, torch.float8_e4m3fn), (k, torch.float8_e4m3fn), (v, pv)):
-        s = torch.clamp(_oracle_absmax_seg(x[None], seg=seg), min=1e-12) / 448.0      # [nseq, H]
+        s = (torch.clamp(_oracle_absmax_seg(x[None], seg=seg), min=1e-12).double() / 448.0).float()  # [nseq, H]
         ops_in.append(_oracle_quant_seg(x[None], s, 1, dt, seg=seg)[0, 0])
         scales.append(s[..., None])
     o = _oracle_attn_varlen(*ops_in, *scales, OA.LOG2E / math.sqrt(D), cu_seqlens=seg)

@@ -111,7 +111,7 @@ def test_ulysses_two_gpus_bit_identical(tmp_path):
     ops_in = []
     scales = []
     for x, dt in ((q, torch.float8_e4m3fn), (k, torch.float8_e4m3fn), (v, torch.float16)):
-        s = torch.clamp(x.float().abs().amax(dim=(1, 3)), min=1e-12) / 448.0
+        s = (torch.clamp(x.float().abs().amax(dim=(1, 3)), min=1e-12).double() / 448.0).float()
         y = x.float() / s[:, None, :, None]
         if dt == torch.float8_e4m3fn:
             y = torch.clamp(y, -448, 448)
