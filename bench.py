@@ -765,10 +765,10 @@ def linear_results(M, steps, warmup):
 
 
 def run_varlen_workload(args):
-    print(json.dumps(varlen_results(args.steps, args.warmup)), flush=True)
+    print(json.dumps(varlen_results(args.steps, args.warmup, args.heads)), flush=True)
 
 
-def varlen_results(steps, warmup):
+def varlen_results(steps, warmup, heads=40):
     """Benchmark configuration 3: packed varlen, cu_seqlens [0, 33784, 50676], H=40 D=128.
 
     e4m3 q/k/v with per-(sequence, head) scales (synthetic N(0,1) with one
@@ -780,7 +780,7 @@ def varlen_results(steps, warmup):
     dev = torch.device("cuda", 0)
     stream = torch.cuda.current_stream(dev)
     lens = [33784, 16892]
-    T, Hh, Dd = sum(lens), 40, 128
+    T, Hh, Dd = sum(lens), heads, 128
     g = torch.Generator(device=dev).manual_seed(0)
     gc = torch.Generator().manual_seed(0)
     cu = torch.tensor([0, lens[0], T], dtype=torch.int32, device=dev)
@@ -817,7 +817,7 @@ def varlen_results(steps, warmup):
     del qkv
     flop = 4.0 * Hh * Dd * sum(L * L for L in lens)
     peaks = _peaks()
-    return {"workload": "config3: varlen cu_seqlens [0,33784,50676], H=40 D=128, per-(seq,head) "
+    return {"workload": f"config3: varlen cu_seqlens [0,33784,50676], H={Hh} D=128, per-(seq,head) "
                         "scales, f16 PV", "unit": "TFLOP/s", "ms": ms, "tflops": flop / ms / 1e9,
             "frac_of_fp8_peak": flop / ms / 1e9 / peaks["fp8_tflops"], "flop": flop,
             "dropin_ms": ms_dropin, "dropin_tflops": flop / ms_dropin / 1e9,
