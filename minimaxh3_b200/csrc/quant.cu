@@ -478,12 +478,26 @@ __global__ void __launch_bounds__(kThreads) bh_absmax_kernel(const T* __restrict
   if (r0 >= last) return;                       // uniform over the CTA
   const int r1 = min(last, r0 + kStatRows);
   const T* xp = x + (SEG ? 0 : b * sb) + h * sh + cg * 8;
+  // 16-byte loads issued kBatch at a time (several in flight per thread),
+  // rows past the chunk read as zeros.
+  constexpr int kPass = kStatRows / RL;
+  constexpr int kBatch = 4;
   float m = 0.0f;
-  for (int r = r0 + rl; r < r1; r += RL) {
-    float v[8];
-    load8(xp + (long long)r * ss, v);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
+  for (int k0 = 0; k0 < kPass; k0 += kBatch) {
+    uint4 u[kBatch];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      const int r = r0 + rl + (k0 + i) * RL;
+      u[i] = r < r1 ? *reinterpret_cast<const uint4*>(xp + (long long)r * ss) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      float v[8];
+      unpack8<T>(u[i], v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(v[e]));
+    }
   }
   m = block_max(m, red);
   if (threadIdx.x == 0) atomicMax(reinterpret_cast<int*>(amax) + (long long)b * gridDim.y + j, __float_as_int(m));
@@ -492,49 +506,75 @@ __global__ void __launch_bounds__(kThreads) bh_absmax_kernel(const T* __restrict
 // y = x / scale[b, j] (IEEE division) for the selected heads, e4m3 (clamped
 // to +-448, RNE) or f16 (RNE), written block-major: out [P, B, S, hs, D] with
 // P = H/hb and selected head j = p*hs + i at [p, b, s, i] - the send buffer of
-// a head-parallel all-to-all (all heads, hb = H: plain [B, S, H, D]).  One
-// thread per 8 channels.  SEG (B = 1): row s takes the scale of its segment
-// z, scale[z, j]; rows outside every segment are written as zeros.
-template <typename T, bool OUT_F16, bool SEG>
+// a head-parallel all-to-all (all heads, hb = H: plain [B, S, H, D]).  SEG
+// (B = 1): row s takes the scale of its segment z, scale[z, j]; rows outside
+// every segment are written as zeros.  Grid (row chunk, j, b): one CTA per
+// kQuantRows rows of one selected head, one thread per 8 channels of a row;
+// each thread first issues all its row loads, then converts and stores.
+constexpr int kQuantRows = 128;
+
+template <typename T, int D, bool OUT_F16, bool SEG>
 __global__ void __launch_bounds__(kThreads) bh_quant_kernel(const T* __restrict__ x, long long sb, long long ss,
-                                                           long long sh, int B, int S, int H, int D, HeadSel sel,
-                                                           Segs segs, const float* __restrict__ scale,
+                                                           long long sh, int S, HeadSel sel, Segs segs,
+                                                           const float* __restrict__ scale,
                                                            uint8_t* __restrict__ out) {
-  const int CG = D / 8;
-  const int nsel = (H / sel.hb) * sel.hs;
-  const long long n = (long long)B * S * nsel * CG;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const int g = (int)(i % CG);
-    long long t = i / CG;
-    const int j = (int)(t % nsel);
-    t /= nsel;
-    const int s = (int)(t % S);
-    const int b = (int)(t / S);
-    const int h = sel.head(j);
-    const int z = SEG ? segs.find(s, S) : b;
-    float y[8];
-    if (z >= 0) {
-      float v[8];
-      load8(x + b * sb + (long long)s * ss + h * sh + g * 8, v);
-      const float sc = __ldg(scale + (long long)z * nsel + j);
-      const float rc = __frcp_rn(sc);
+  constexpr int CG = D / 8;
+  constexpr int RPI = kThreads / CG;         // rows per pass
+  constexpr int kPass = kQuantRows / RPI;
+  constexpr int ES = OUT_F16 ? 2 : 1;
+  const int j = blockIdx.y, b = blockIdx.z;
+  const int nsel = gridDim.y, B = gridDim.z;
+  const int h = sel.head(j);
+  const int p = j / sel.hs, hl = j - p * sel.hs;
+  const int g = threadIdx.x % CG;
+  const int s0 = blockIdx.x * kQuantRows + threadIdx.x / CG;
+  const T* xp = x + b * sb + h * sh + g * 8;
+  const long long orow = (long long)sel.hs * D;  // output elements from one row to the next
+  uint8_t* op = out + ((((long long)p * B + b) * S) * orow + (long long)hl * D + g * 8) * ES;
+  uint4 u[kPass];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) y[k] = div_rn_by(v[k], sc, rc);  // e4m3: clamp by cvt.satfinite
-    } else {
+  for (int k = 0; k < kPass; ++k) {
+    const int s = s0 + k * RPI;
+    u[k] = s < S ? *reinterpret_cast<const uint4*>(xp + (long long)s * ss) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float sc = 1.0f, rc = 1.0f;
+  if constexpr (!SEG) {
+    sc = __ldg(scale + (long long)b * nsel + j);
+    rc = __frcp_rn(sc);
+  }
 #pragma unroll
-      for (int k = 0; k < 8; ++k) y[k] = 0.0f;
+  for (int k = 0; k < kPass; ++k) {
+    const int s = s0 + k * RPI;
+    if (s >= S) break;
+    bool live = true;
+    if constexpr (SEG) {
+      const int z = segs.find(s, S);
+      live = z >= 0;
+      if (live) {
+        sc = __ldg(scale + (long long)z * nsel + j);
+        rc = __frcp_rn(sc);
+      }
     }
-    const int p = j / sel.hs, hl = j - p * sel.hs;
-    const long long o = ((((long long)p * B + b) * S + s) * sel.hs + hl) * D + g * 8;
-    if constexpr (OUT_F16) {
-      uint4 u;
-      u.x = cvt_f16x2(y[1], y[0]);
-      u.y = cvt_f16x2(y[3], y[2]);
-      u.z = cvt_f16x2(y[5], y[4]);
-      u.w = cvt_f16x2(y[7], y[6]);
-      *reinterpret_cast<uint4*>(out + o * 2) = u;
+    float y[8];
+    if (live) {
+      float v[8];
+      unpack8<T>(u[k], v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[e] = div_rn_by(v[e], sc, rc);  // e4m3: clamp by cvt.satfinite
     } else {
-      *reinterpret_cast<uint2*>(out + o) = pack8_e4m3(y);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[e] = 0.0f;
+    }
+    uint8_t* dst = op + (long long)s * orow * ES;
+    if constexpr (OUT_F16) {
+      uint4 w;
+      w.x = cvt_f16x2(y[1], y[0]);
+      w.y = cvt_f16x2(y[3], y[2]);
+      w.z = cvt_f16x2(y[5], y[4]);
+      w.w = cvt_f16x2(y[7], y[6]);
+      *reinterpret_cast<uint4*>(dst) = w;
+    } else {
+      *reinterpret_cast<uint2*>(dst) = pack8_e4m3(y);
     }
   }
 }
@@ -554,6 +594,36 @@ bool bh_shape_ok(const void* x, int32_t in_dtype, int64_t B, int64_t S, int64_t 
   if (((uintptr_t)x & 15u) || (sb % 8) || (ss % 8) || (sh % 8))
     return (*why = "x must be 16-byte aligned with strides multiple of 8 elements"), false;
   return true;
+}
+
+template <typename T, int D, bool F16>
+void launch_bh_quant_t(const void* x, int64_t sb, int64_t ss, int64_t sh, quant::HeadSel sel, quant::Segs segs,
+                       const float* scale, void* out, dim3 grid, int S, bool seg, cudaStream_t st) {
+  const T* xt = static_cast<const T*>(x);
+  uint8_t* o = static_cast<uint8_t*>(out);
+  if (seg)
+    quant::bh_quant_kernel<T, D, F16, true><<<grid, quant::kThreads, 0, st>>>(xt, sb, ss, sh, S, sel, segs, scale, o);
+  else
+    quant::bh_quant_kernel<T, D, F16, false><<<grid, quant::kThreads, 0, st>>>(xt, sb, ss, sh, S, sel, segs, scale, o);
+}
+
+// Launches bh_quant_kernel for the dtypes and head dim; returns true when the launch failed.
+bool launch_bh_quant(const void* x, int32_t in_dtype, int64_t D, int64_t sb, int64_t ss, int64_t sh,
+                     quant::HeadSel sel, quant::Segs segs, const float* scale, int32_t out_dtype, void* out, dim3 grid,
+                     int S, bool seg, cudaStream_t st) {
+  const bool f16 = out_dtype == MH3_DTYPE_F16;
+  const bool bf = in_dtype == MH3_DTYPE_BF16;
+#define MH3_BHQ(T, DD, F)                                                                  \
+  launch_bh_quant_t<T, DD, F>(x, sb, ss, sh, sel, segs, scale, out, grid, S, seg, st)
+  if (D == 128) {
+    if (bf) { if (f16) MH3_BHQ(__nv_bfloat16, 128, true); else MH3_BHQ(__nv_bfloat16, 128, false); }
+    else { if (f16) MH3_BHQ(__half, 128, true); else MH3_BHQ(__half, 128, false); }
+  } else {
+    if (bf) { if (f16) MH3_BHQ(__nv_bfloat16, 64, true); else MH3_BHQ(__nv_bfloat16, 64, false); }
+    else { if (f16) MH3_BHQ(__half, 64, true); else MH3_BHQ(__half, 64, false); }
+  }
+#undef MH3_BHQ
+  return cudaPeekAtLastError() != cudaSuccess;
 }
 }  // namespace
 
@@ -598,21 +668,12 @@ extern "C" int mh3_quantize_bh(const void* x, int32_t in_dtype, int64_t B, int64
   const quant::HeadSel sel{head_block, head_off, heads_sel};
   if ((uintptr_t)out & 15u) return fail(MH3_ERR_INVALID, "mh3_quantize_bh: out must be 16-byte aligned");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const long long n = B * S * (H / head_block) * heads_sel * (D / 8);
-  const int blocks = (int)std::min<long long>((n + quant::kThreads - 1) / quant::kThreads, 148ll * 16);
-  uint8_t* o = static_cast<uint8_t*>(out);
-#define MH3_BHQ(T, F16)                                                                                      \
-  quant::bh_quant_kernel<T, F16, false><<<blocks, quant::kThreads, 0, st>>>(                                   \
-      static_cast<const T*>(x), sb, ss, sh, (int)B, (int)S, (int)H, (int)D, sel, quant::Segs{nullptr, 0}, scale, o)
-  const bool f16 = out_dtype == MH3_DTYPE_F16;
-  if (in_dtype == MH3_DTYPE_BF16) {
-    if (f16) MH3_BHQ(__nv_bfloat16, true); else MH3_BHQ(__nv_bfloat16, false);
-  } else {
-    if (f16) MH3_BHQ(__half, true); else MH3_BHQ(__half, false);
-  }
-#undef MH3_BHQ
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? MH3_OK : fail_cuda(e, "mh3_quantize_bh launch");
+  const dim3 grid((unsigned)((S + quant::kQuantRows - 1) / quant::kQuantRows),
+                  (unsigned)((H / head_block) * heads_sel), (unsigned)B);
+  return launch_bh_quant(x, in_dtype, D, sb, ss, sh, sel, quant::Segs{nullptr, 0}, scale, out_dtype, out, grid, (int)S,
+                         false, st)
+             ? fail_cuda(cudaGetLastError(), "mh3_quantize_bh launch")
+             : MH3_OK;
 }
 
 extern "C" int mh3_absmax_seg(const void* x, int32_t in_dtype, int64_t S, int64_t H, int64_t D, int64_t ss,
@@ -662,22 +723,12 @@ extern "C" int mh3_quantize_seg(const void* x, int32_t in_dtype, int64_t S, int6
   const quant::HeadSel sel{head_block, head_off, heads_sel};
   if ((uintptr_t)out & 15u) return fail(MH3_ERR_INVALID, "mh3_quantize_seg: out must be 16-byte aligned");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const long long n = S * (H / head_block) * heads_sel * (D / 8);
-  const int blocks = (int)std::min<long long>((n + quant::kThreads - 1) / quant::kThreads, 148ll * 16);
-  const quant::Segs segs{seg, nseg};
-  uint8_t* o = static_cast<uint8_t*>(out);
-#define MH3_SEGQ(T, F16)                                                                                   \
-  quant::bh_quant_kernel<T, F16, true><<<blocks, quant::kThreads, 0, st>>>(static_cast<const T*>(x), 0, ss, sh, 1, \
-                                                                           (int)S, (int)H, (int)D, sel, segs, scale, o)
-  const bool f16 = out_dtype == MH3_DTYPE_F16;
-  if (in_dtype == MH3_DTYPE_BF16) {
-    if (f16) MH3_SEGQ(__nv_bfloat16, true); else MH3_SEGQ(__nv_bfloat16, false);
-  } else {
-    if (f16) MH3_SEGQ(__half, true); else MH3_SEGQ(__half, false);
-  }
-#undef MH3_SEGQ
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? MH3_OK : fail_cuda(e, "mh3_quantize_seg launch");
+  const dim3 grid((unsigned)((S + quant::kQuantRows - 1) / quant::kQuantRows),
+                  (unsigned)((H / head_block) * heads_sel), 1u);
+  return launch_bh_quant(x, in_dtype, D, 0, ss, sh, sel, quant::Segs{seg, nseg}, scale, out_dtype, out, grid, (int)S,
+                         true, st)
+             ? fail_cuda(cudaGetLastError(), "mh3_quantize_seg launch")
+             : MH3_OK;
 }
 
 extern "C" uint64_t mh3_qkv_workspace_bytes(int32_t batch, int32_t heads, int32_t seqlen_k, int32_t head_dim) {
