@@ -764,6 +764,61 @@ def linear_results(M, steps, warmup):
             if RL is not None else f"unavailable: {ref_missing}", "results": lines}
 
 
+def run_bf16_gemm_workload(args):
+    """Unquantised bf16 linear (+ LoRA r=32) against cuBLAS at config 4's shapes, M = --linear-rows.
+
+    Interleaved timing (5 rounds, each function 5 calls per round, medians) of: this package's
+    bf16 main GEMM, the same with the LoRA K-steps, the LoRA-down product, ``ops.linear_lora``,
+    cuBLAS ``F.linear`` and the reference recipe (``F.linear`` + LoRA matmuls + add).  Then one
+    more call of the main GEMM and of ``F.linear`` at N=K=5120 between cudaProfilerStart/Stop,
+    the pair an ``ncu --profile-from-start off -c 2`` capture compares.
+    """
+    import statistics
+
+    from minimaxh3_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev)
+    M = args.linear_rows
+    g = torch.Generator(device=dev).manual_seed(0)
+    results = {}
+    keep = None
+    for N, K in ((13824, 5120), (5120, 13824), (5120, 5120)):
+        x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+        w = (torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        bias = (torch.randn(N, generator=g, device=dev) * 0.01).to(torch.bfloat16)
+        A = (torch.randn(32, K, generator=g, device=dev) * 0.01).to(torch.bfloat16)
+        Bm = (torch.randn(N, 32, generator=g, device=dev) * 0.01).to(torch.bfloat16)
+        a2 = ops.scaled_gemm(x, A)
+        fns = {
+            "mh3_main_gemm": lambda: ops.scaled_gemm(x, w, bias=bias),
+            "mh3_main_gemm_with_lora_ksteps": lambda: ops.scaled_gemm(x, w, bias=bias, a2=a2, b2=Bm),
+            "mh3_lora_down": lambda: ops.scaled_gemm(x, A),
+            "mh3_linear_lora": lambda: ops.linear_lora(x, w, bias, [(A, Bm, 1.0)]),
+            "cublas_linear": lambda: torch.nn.functional.linear(x, w, bias),
+            "reference_recipe": lambda: torch.nn.functional.linear(x, w, bias) + ((x @ A.t()) @ Bm.t()),
+        }
+        samples = {k: [] for k in fns}
+        for _ in range(5):
+            for k, fn in fns.items():
+                samples[k].append(_time_cuda(fn, 5, 1, stream))
+        flop = 2.0 * M * N * K
+        results[f"N={N},K={K}"] = {k: {"ms": statistics.median(v), "tflops": flop / statistics.median(v) / 1e9}
+                                   for k, v in samples.items()}
+        if N == K:
+            keep = (x, w, bias)
+        del a2
+    x, w, bias = keep
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStart()
+    ops.scaled_gemm(x, w, bias=bias)
+    torch.nn.functional.linear(x, w, bias)
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    print(json.dumps({"workload": f"bf16 linear + LoRA r=32 vs cuBLAS, M={M}", "unit": "TFLOP/s",
+                      "results": results}), flush=True)
+
+
 def run_varlen_workload(args):
     print(json.dumps(varlen_results(args.steps, args.warmup, args.heads)), flush=True)
 
@@ -956,7 +1011,7 @@ def main():
     ap.add_argument("--no-extras", action="store_true",
                     help="kernel timing only (no e2e, no CPU baseline): the ncu capture command")
     ap.add_argument("--workload", default="attention",
-                    choices=["attention", "linear", "quant", "varlen", "block", "step"],
+                    choices=["attention", "linear", "quant", "varlen", "block", "step", "bf16_gemm"],
                     help="attention = config 2 (the headline line); linear = config 4 measurements")
     ap.add_argument("--pv", default="f16", choices=["f16", "e4m3"],
                     help="PV product operands: f16 P/V (default, meets the tolerance) or e4m3")
@@ -987,6 +1042,9 @@ def main():
         return
     if args.workload == "linear":
         run_linear_workload(args)
+        return
+    if args.workload == "bf16_gemm":
+        run_bf16_gemm_workload(args)
         return
     dist, rank, world, local = _dist()
     try:
