@@ -50,8 +50,10 @@ the world size is padded by the caller with tokens past the last sequence.
 memory: each group's heads are copied in (one strided copy per tensor) on
 one stream and copied back on another, overlapping the other groups'
 compute; it optionally computes the block's cross-attention to replicated
-text K/V per group as well.  Cross-attention alone needs no collective: call
-``fp8_attention`` on the local query shard.
+text K/V per group as well.  Cross-attention needs no collective (it is
+``fp8_attention`` of the local query shard); ``ulysses_attention(...,
+cross_kv=)`` issues it right after the first input all-to-all, so NCCL's
+exchange runs on a few SMs while the cross-attention takes the rest.
 
 ``attn_fn``, ``absmax_fn`` and ``quant_fn`` are injectable so the collective
 plumbing can be tested on CPU ``gloo`` ranks with the oracle standing in for
@@ -275,7 +277,7 @@ class _Pipeline:
         recv_o, w = _exchange_async(send_o, self.group)
         return recv_o, (w, send_o)
 
-    def run(self, G, source, sink, on_quantized=None):
+    def run(self, G, source, sink, on_quantized=None, before_first_attention=None):
         a, b, c = {}, {}, {}
 
         def stage_a(g):
@@ -305,6 +307,9 @@ class _Pipeline:
                 stage_a(g + 2)
             if g + 1 < G:
                 stage_b(g + 1)
+            if g == 0 and before_first_attention is not None:
+                # local work issued here runs while the first exchanges are in flight
+                before_first_attention()
             stage_c(g)
             if g >= 1:
                 stage_d(g - 1)
@@ -320,12 +325,18 @@ def _packing(cu_seqlens, P, r, B, S_l, device):
 
 
 def ulysses_attention(q, k, v, group=None, scale=None, pv_dtype=torch.float16, attn_fn=None, events=None,
-                      absmax_fn=None, quant_fn=None, head_groups=1, out=None, cu_seqlens=None):
+                      absmax_fn=None, quant_fn=None, head_groups=1, out=None, cu_seqlens=None, cross_kv=None):
     """Head-parallel FP8 attention of sequence shards ``[B, S_local, H, D]``.
 
     Returns the local output shard ``[B, S_local, H, D]`` (q's dtype; written
     into ``out`` when given, contiguous).  H must be divisible by the world
     size P and H/P by ``head_groups``; every rank must hold the same S_local.
+    ``cross_kv``: optional (k_text, v_text) CUDA tensors ``[B, H, T, D]``
+    replicated on every rank; the block's cross-attention of the local query
+    shard (``fp8_attention``, no collective) is then issued right after the
+    first input all-to-all, so that exchange runs while it computes, and the
+    call returns ``(out, cross)`` with ``cross`` ``[B, S_local, H, D]`` (a
+    view of a ``[B, H, S_local, D]``-strided tensor).
     ``cu_seqlens``: global offsets (host ints: a list or a CPU tensor, the same
     on every rank) of sequences packed along S of a batch-1 input; attention
     then stays inside each sequence, with per-(sequence, head) scales.
@@ -359,8 +370,18 @@ def ulysses_attention(q, k, v, group=None, scale=None, pv_dtype=torch.float16, a
 
     pipe = _Pipeline(P, r, Hg, (B, S_l, D), q.dtype, group, pv_dtype, ls2, attn_fn, absmax_fn, quant_fn, events,
                      packing)
-    pipe.run(head_groups, source, sink)
-    return out
+    cross = []
+
+    def cross_attention():
+        from .kernels.fp8_attention import fp8_attention
+
+        kt, vt = cross_kv
+        cross.append(fp8_attention(q.transpose(1, 2), kt, vt, scale=scale).transpose(1, 2))
+
+    if cross_kv is not None and packing is not None:
+        raise ValueError("cross_kv is not supported with cu_seqlens")
+    pipe.run(head_groups, source, sink, before_first_attention=cross_attention if cross_kv is not None else None)
+    return out if cross_kv is None else (out, cross[0])
 
 
 class _HostShardBuffers:

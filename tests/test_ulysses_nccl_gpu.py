@@ -75,12 +75,15 @@ def _worker(rank, world, port, shape, out_dir):
         hq, hk, hv = (t.cpu().pin_memory() for t in shard)
         ho, hc = ulysses_attention_host(hq, hk, hv, head_groups=2, cross_kv=(kt, vt))
         cross = fp8_attention(shard[0].transpose(1, 2), kt, vt).transpose(1, 2)
+        # the device path with the cross-attention issued during the first exchange
+        dev_o, dev_c = ulysses_attention(*shard, head_groups=2, cross_kv=(kt, vt))
         torch.cuda.synchronize()
         hp = ulysses_attention_host(hq, hk, hv, head_groups=2, cu_seqlens=PACKED_CU)
         torch.cuda.synchronize()
         torch.save({"out": {G: o.cpu() for G, o in outs.items()}, "host": ho.clone(), "host_cross": hc.clone(),
                     "cross": cross.cpu(), "packed": {G: o.cpu() for G, o in packed.items()},
-                    "host_packed": hp.clone()}, os.path.join(out_dir, f"out{rank}.pt"))
+                    "host_packed": hp.clone(), "dev_cross": (dev_o.cpu(), dev_c.cpu())},
+                   os.path.join(out_dir, f"out{rank}.pt"))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -106,6 +109,8 @@ def test_ulysses_two_gpus_bit_identical(tmp_path):
             assert torch.equal(x["out"][G], x["out"][1])
         assert torch.equal(x["host"], x["out"][1])         # host-resident variant
         assert torch.equal(x["host_cross"], x["cross"])    # its per-group cross-attention
+        assert torch.equal(x["dev_cross"][0], x["out"][1])  # device path with cross_kv
+        assert torch.equal(x["dev_cross"][1], x["cross"])
     # one GPU, whole sequence, same global per-(b,h) scales
     q, k, v = (t.cuda() for t in _inputs(B, S, H, D))
     ops_in = []
@@ -146,6 +151,7 @@ def _single_rank_worker(port, out_dir):
         kt, vt = (torch.randn(B, H, 256, D, generator=gt).to(torch.bfloat16).cuda() for _ in range(2))
         dev_out = ulysses_attention(q, k, v)
         cross = fp8_attention(q.transpose(1, 2), kt, vt).transpose(1, 2)
+        dev_o, dev_c = ulysses_attention(q, k, v, head_groups=4, cross_kv=(kt, vt))
         hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
         res = []
         for G in (4, 4, 2):                      # the second call reuses the first one's device buffers
@@ -157,6 +163,7 @@ def _single_rank_worker(port, out_dir):
         packed_host = ulysses_attention_host(hq, hk, hv, head_groups=2, cu_seqlens=torch.tensor(cu))
         torch.cuda.synchronize()
         torch.save({"dev": dev_out.cpu(), "cross": cross.cpu(), "host": res, "packed": packed.cpu(),
+                    "dev_cross": (dev_o.cpu(), dev_c.cpu()),
                     "packed_host": packed_host.clone(), "packed_ref": _packed_single_gpu(q, k, v, cu).cpu()},
                    os.path.join(out_dir, "single.pt"))
     finally:
@@ -176,6 +183,7 @@ def test_host_resident_pipeline_on_one_rank(tmp_path):
     for o, c in r["host"]:
         assert torch.equal(o, r["dev"])
         assert torch.equal(c, r["cross"])
+    assert torch.equal(r["dev_cross"][0], r["dev"]) and torch.equal(r["dev_cross"][1], r["cross"])
     assert torch.equal(r["packed"], r["packed_ref"])          # Ulysses with cu_seqlens = the drop-in varlen path
     assert torch.equal(r["packed_host"], r["packed_ref"])
     assert torch.count_nonzero(r["packed"][0, 900:]) == 0
