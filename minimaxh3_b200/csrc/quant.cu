@@ -542,18 +542,28 @@ __global__ void __launch_bounds__(kThreads) bh_quant_kernel(const T* __restrict_
     sc = __ldg(scale + (long long)b * nsel + j);
     rc = __frcp_rn(sc);
   }
+  // SEG: a thread's rows only move forward, so it keeps the row range
+  // [zlo, zhi) of the sequence whose scale it holds and looks a sequence up
+  // again only when a row leaves that range.
+  int zlo = 0, zhi = 0;
 #pragma unroll
   for (int k = 0; k < kPass; ++k) {
     const int s = s0 + k * RPI;
     if (s >= S) break;
     bool live = true;
     if constexpr (SEG) {
-      const int z = segs.find(s, S);
-      live = z >= 0;
-      if (live) {
-        sc = __ldg(scale + (long long)z * nsel + j);
-        rc = __frcp_rn(sc);
+      if (s < zlo || s >= zhi) {
+        const int z = segs.find(s, S);
+        if (z >= 0) {
+          zlo = segs.bound(z, S);
+          zhi = segs.bound(z + 1, S);
+          sc = __ldg(scale + (long long)z * nsel + j);
+          rc = __frcp_rn(sc);
+        } else {
+          zlo = zhi = 0;
+        }
       }
+      live = s >= zlo && s < zhi;
     }
     float y[8];
     if (live) {
