@@ -408,8 +408,9 @@ def run_ulysses_arm(args, dist, rank, world, local):
     o_buf = torch.empty_like(q)
 
     def step(ev=None):
-        # the cross-attention runs while the input all-to-all is in flight
-        return ulysses_attention(q, k, v, events=ev, head_groups=G, out=o_buf, cross_kv=(kt, vt))
+        # the cross-attention runs while the input exchange is in flight
+        return ulysses_attention(q, k, v, events=ev, head_groups=G, out=o_buf, cross_kv=(kt, vt),
+                                 exchange=args.exchange)
 
     for _ in range(args.warmup):
         step()
@@ -473,6 +474,7 @@ def run_ulysses_arm(args, dist, rank, world, local):
         "config": {"workload": f"config5: Ulysses self-attention B=1 H=40 S=75600 D=128 over {world} GPUs "
                                f"(S/P={Sl}, H/P={H5 // world}) + cross-attention to 512 text tokens",
                    "parallelism": f"ulysses{world}", "head_groups": G, "e2e_head_groups": G_host,
+                   "exchange": args.exchange,
                    "inputs_vs_l2": "per-rank inputs > 126 MB L2 (no flush)"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["fp8_tflops"], "unit": "TFLOP/s",
                      "frac": achieved / peaks["fp8_tflops"], "traffic": None, "peak_source": peaks["source"],
@@ -1016,6 +1018,8 @@ def main():
                     help="PV product operands: f16 P/V (default, meets the tolerance) or e4m3")
     ap.add_argument("--linear-rows", type=int, default=32760,
                     help="linear workload: token rows M (32760 = config 4; smaller for ncu captures)")
+    ap.add_argument("--exchange", default="nccl", choices=["nccl", "peer"],
+                    help="N>1: Ulysses exchange by NCCL all-to-alls or by copy-engine pulls from peer buffers")
     ap.add_argument("--head-groups", type=int, default=1,
                     help="N>1: head groups of the device-resident Ulysses pipeline (the value line)")
     ap.add_argument("--host-head-groups", type=int, default=0,

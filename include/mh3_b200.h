@@ -36,8 +36,9 @@ extern "C" {
  * 2: mh3_attn_args.kv_len; 3: head selection in mh3_absmax_bh /
  * mh3_quantize_bh, mh3_copy_rows, mh3_step_diff; 4: f32 input to
  * mh3_quantize_rows, test_flags in mh3_attn_args (was reserved0) and
- * mh3_gemm_args; 5: mh3_absmax_seg, mh3_quantize_seg. */
-#define MH3_ABI_VERSION 5
+ * mh3_gemm_args; 5: mh3_absmax_seg, mh3_quantize_seg; 6: mh3_peer_alloc,
+ * mh3_peer_free, mh3_peer_handle, mh3_peer_open, mh3_peer_close. */
+#define MH3_ABI_VERSION 6
 
 #define MH3_OK 0
 #define MH3_ERR_INVALID (-1)     /* bad argument: shape, stride, alignment, null pointer */
@@ -315,12 +316,35 @@ MH3_API int mh3_quantize_seg(const void* x, int32_t in_dtype, int64_t S, int64_t
                              int32_t nseg, const float* scale, int32_t out_dtype, void* out, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Exchange buffers shared between processes (CUDA IPC)                     */
+/* ------------------------------------------------------------------------ */
+/*
+ * For a head-parallel exchange over copy engines: each rank allocates its
+ * send buffers with mh3_peer_alloc (one device allocation each, on the
+ * current device), exports them with mh3_peer_handle (MH3_PEER_HANDLE_BYTES
+ * opaque bytes, to be passed to the other processes of the node), and maps a
+ * peer's buffer with mh3_peer_open, which returns a pointer valid on the
+ * current device (peer access enabled on first use).  Chunks are then
+ * pulled with mh3_copy_rows.  mh3_peer_handle needs the pointer
+ * mh3_peer_alloc returned.  Close every mapping (mh3_peer_close) before the
+ * owner frees the buffer (mh3_peer_free).  Plain peer mappings only; no
+ * multicast object is created.  No reference counterpart.
+ */
+#define MH3_PEER_HANDLE_BYTES 64
+MH3_API int mh3_peer_alloc(int64_t bytes, void** ptr);
+MH3_API int mh3_peer_free(void* ptr);
+MH3_API int mh3_peer_handle(const void* ptr, void* handle);
+MH3_API int mh3_peer_open(const void* handle, void** ptr);
+MH3_API int mh3_peer_close(void* ptr);
+
+/* ------------------------------------------------------------------------ */
 /* Strided host<->device row copies                                         */
 /* ------------------------------------------------------------------------ */
 /*
  * rows x row_bytes from src (row pitch src_pitch bytes) to dst (row pitch
  * dst_pitch bytes), asynchronously on ``stream``, either direction between
- * pinned host memory and device memory (or device to device).  Moves one
+ * pinned host memory and device memory, or device to device (also from a
+ * peer's buffer mapped with mh3_peer_open: a copy-engine copy).  Moves one
  * head group of a host-resident [B, S, H, D] shard - a run of heads in every
  * token row - without staging it through a contiguous host copy.  No
  * reference counterpart (the reference's tensors are device-resident).

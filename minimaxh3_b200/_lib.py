@@ -23,6 +23,7 @@ MH3_DTYPE_F16 = 1
 MH3_DTYPE_E4M3 = 2
 MH3_DTYPE_F32 = 3
 MH3_DEVERR_WAIT_TIMEOUT = 1
+MH3_PEER_HANDLE_BYTES = 64
 MH3_TEST_STALL_PRODUCER = 1
 
 c_i32 = ctypes.c_int32
@@ -104,6 +105,11 @@ _SIGNATURES = {
     "mh3_quantize_seg": (c_i32, [c_ptr, c_i32, c_i64, c_i64, c_i64, c_i64, c_i64, c_i32, c_i32, c_i32, c_ptr, c_i32,
                                  c_ptr, c_i32, c_ptr, c_ptr]),
     "mh3_copy_rows": (c_i32, [c_ptr, c_i64, c_ptr, c_i64, c_i64, c_i64, c_ptr]),
+    "mh3_peer_alloc": (c_i32, [c_i64, c_ptr]),
+    "mh3_peer_free": (c_i32, [c_ptr]),
+    "mh3_peer_handle": (c_i32, [c_ptr, c_ptr]),
+    "mh3_peer_open": (c_i32, [c_ptr, c_ptr]),
+    "mh3_peer_close": (c_i32, [c_ptr]),
     "mh3_step_diff_workspace_bytes": (c_u64, []),
     "mh3_step_diff": (c_i32, [c_ptr, c_ptr, c_i32, c_i64, c_i32, c_ptr, c_ptr, c_ptr]),
 }

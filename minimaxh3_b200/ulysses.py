@@ -325,7 +325,8 @@ def _packing(cu_seqlens, P, r, B, S_l, device):
 
 
 def ulysses_attention(q, k, v, group=None, scale=None, pv_dtype=torch.float16, attn_fn=None, events=None,
-                      absmax_fn=None, quant_fn=None, head_groups=1, out=None, cu_seqlens=None, cross_kv=None):
+                      absmax_fn=None, quant_fn=None, head_groups=1, out=None, cu_seqlens=None, cross_kv=None,
+                      exchange="nccl"):
     """Head-parallel FP8 attention of sequence shards ``[B, S_local, H, D]``.
 
     Returns the local output shard ``[B, S_local, H, D]`` (q's dtype; written
@@ -337,6 +338,10 @@ def ulysses_attention(q, k, v, group=None, scale=None, pv_dtype=torch.float16, a
     first input all-to-all, so that exchange runs while it computes, and the
     call returns ``(out, cross)`` with ``cross`` ``[B, S_local, H, D]`` (a
     view of a ``[B, H, S_local, D]``-strided tensor).
+    ``exchange``: ``"nccl"`` (NCCL all-to-alls) or ``"peer"`` (copy-engine
+    pulls from the peers' buffers mapped through CUDA IPC,
+    ``peer_exchange.ulysses_attention_peer``: batch 1, one head group, no
+    ``cu_seqlens``, the CUDA kernels; same result bit for bit).
     ``cu_seqlens``: global offsets (host ints: a list or a CPU tensor, the same
     on every rank) of sequences packed along S of a batch-1 input; attention
     then stays inside each sequence, with per-(sequence, head) scales.
@@ -348,6 +353,15 @@ def ulysses_attention(q, k, v, group=None, scale=None, pv_dtype=torch.float16, a
     segment bounds) and attn_fn ``cu_seqlens=`` / ``max_seqlen=`` for a packed
     batch).
     """
+    if exchange == "peer":
+        if head_groups != 1 or cu_seqlens is not None or attn_fn or absmax_fn or quant_fn:
+            raise ValueError("exchange='peer' takes one head group, no cu_seqlens and the CUDA kernels")
+        from .peer_exchange import ulysses_attention_peer
+
+        return ulysses_attention_peer(q, k, v, group=group, scale=scale, pv_dtype=pv_dtype, out=out,
+                                      cross_kv=cross_kv, events=events)
+    if exchange != "nccl":
+        raise ValueError("exchange must be 'nccl' or 'peer'")
     P, r = _world(group)
     B, S_l, H, D = q.shape
     _check_heads(H, P, head_groups)

@@ -35,7 +35,7 @@ def test_binding_covers_header():
 
 def test_host_only_calls():
     lib = _lib.load()
-    assert lib.mh3_abi_version() == 5
+    assert lib.mh3_abi_version() == 6
     assert lib.mh3_qkv_workspace_bytes(1, 40, 32760, 128) == 2 * 40 * 128 * 128 * 4
     assert lib.mh3_qkv_workspace_bytes(0, 1, 1, 128) == 0
 

@@ -54,3 +54,15 @@ def test_scale_from_absmax_is_the_correctly_rounded_quotient():
     ref = np.maximum(amax.numpy(), np.float32(1e-12)) / np.float32(448.0)   # numpy float32: IEEE division
     assert got.dtype == torch.float32
     assert np.array_equal(got.numpy(), ref)
+
+
+def test_ulysses_exchange_argument_is_checked_before_any_collective():
+    from minimaxh3_b200.ulysses import ulysses_attention
+
+    x = torch.zeros(1, 8, 4, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        ulysses_attention(x, x, x, exchange="shared")
+    with pytest.raises(ValueError):
+        ulysses_attention(x, x, x, exchange="peer", head_groups=2)
+    with pytest.raises(ValueError):
+        ulysses_attention(x, x, x, exchange="peer", cu_seqlens=[0, 8])

@@ -77,12 +77,15 @@ def _worker(rank, world, port, shape, out_dir):
         cross = fp8_attention(shard[0].transpose(1, 2), kt, vt).transpose(1, 2)
         # the device path with the cross-attention issued during the first exchange
         dev_o, dev_c = ulysses_attention(*shard, head_groups=2, cross_kv=(kt, vt))
+        # the copy-engine exchange through the peers' mapped buffers (both send sets)
+        peer = [ulysses_attention(*shard, exchange="peer", cross_kv=(kt, vt)) for _ in range(3)]
         torch.cuda.synchronize()
         hp = ulysses_attention_host(hq, hk, hv, head_groups=2, cu_seqlens=PACKED_CU)
         torch.cuda.synchronize()
         torch.save({"out": {G: o.cpu() for G, o in outs.items()}, "host": ho.clone(), "host_cross": hc.clone(),
                     "cross": cross.cpu(), "packed": {G: o.cpu() for G, o in packed.items()},
-                    "host_packed": hp.clone(), "dev_cross": (dev_o.cpu(), dev_c.cpu())},
+                    "host_packed": hp.clone(), "dev_cross": (dev_o.cpu(), dev_c.cpu()),
+                    "peer": [(o.cpu(), c.cpu()) for o, c in peer]},
                    os.path.join(out_dir, f"out{rank}.pt"))
         dist.barrier()
     finally:
@@ -111,6 +114,8 @@ def test_ulysses_two_gpus_bit_identical(tmp_path):
         assert torch.equal(x["host_cross"], x["cross"])    # its per-group cross-attention
         assert torch.equal(x["dev_cross"][0], x["out"][1])  # device path with cross_kv
         assert torch.equal(x["dev_cross"][1], x["cross"])
+        for o, c in x["peer"]:                              # copy-engine exchange
+            assert torch.equal(o, x["out"][1]) and torch.equal(c, x["cross"])
     # one GPU, whole sequence, same global per-(b,h) scales
     q, k, v = (t.cuda() for t in _inputs(B, S, H, D))
     ops_in = []
@@ -152,6 +157,7 @@ def _single_rank_worker(port, out_dir):
         dev_out = ulysses_attention(q, k, v)
         cross = fp8_attention(q.transpose(1, 2), kt, vt).transpose(1, 2)
         dev_o, dev_c = ulysses_attention(q, k, v, head_groups=4, cross_kv=(kt, vt))
+        peer = [ulysses_attention(q, k, v, exchange="peer", cross_kv=(kt, vt)) for _ in range(3)]
         hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
         res = []
         for G in (4, 4, 2):                      # the second call reuses the first one's device buffers
@@ -163,7 +169,7 @@ def _single_rank_worker(port, out_dir):
         packed_host = ulysses_attention_host(hq, hk, hv, head_groups=2, cu_seqlens=torch.tensor(cu))
         torch.cuda.synchronize()
         torch.save({"dev": dev_out.cpu(), "cross": cross.cpu(), "host": res, "packed": packed.cpu(),
-                    "dev_cross": (dev_o.cpu(), dev_c.cpu()),
+                    "dev_cross": (dev_o.cpu(), dev_c.cpu()), "peer": [(o.cpu(), c.cpu()) for o, c in peer],
                     "packed_host": packed_host.clone(), "packed_ref": _packed_single_gpu(q, k, v, cu).cpu()},
                    os.path.join(out_dir, "single.pt"))
     finally:
@@ -184,6 +190,8 @@ def test_host_resident_pipeline_on_one_rank(tmp_path):
         assert torch.equal(o, r["dev"])
         assert torch.equal(c, r["cross"])
     assert torch.equal(r["dev_cross"][0], r["dev"]) and torch.equal(r["dev_cross"][1], r["cross"])
+    for o, c in r["peer"]:
+        assert torch.equal(o, r["dev"]) and torch.equal(c, r["cross"])
     assert torch.equal(r["packed"], r["packed_ref"])          # Ulysses with cu_seqlens = the drop-in varlen path
     assert torch.equal(r["packed_host"], r["packed_ref"])
     assert torch.count_nonzero(r["packed"][0, 900:]) == 0
