@@ -8,14 +8,14 @@
    (two sets, alternating between calls);
 3. barrier A (a one-word NCCL all-reduce on the compute stream): every
    rank's quantisation is done;
-4. on a copy stream, rank r pulls chunk r of every peer's send buffers into
-   its receive buffers (``mh3_copy_rows`` on peer pointers: copy engines, no
-   SM time), while the compute stream runs the block's cross-attention when
-   ``cross_kv`` is given;
+4. on one copy stream per source rank, rank r pulls chunk r of every
+   rank's send buffers into its receive buffers (``mh3_copy_rows`` on peer
+   pointers: copy engines, no SM time), while the compute stream runs the
+   block's cross-attention when ``cross_kv`` is given;
 5. the attention kernel over the Hl local heads, written into this rank's
    exported output buffer ``[P, B, S_l, Hl, D]``;
 6. barrier B: every rank's attention is done;
-7. on the copy stream, rank r pulls chunk r of every peer's output buffer
+7. on the copy streams, rank r pulls chunk r of every rank's output buffer
    straight into its heads of ``out [B, S_l, H, D]`` (one pitched copy per
    peer), and the compute stream waits for it.
 
@@ -105,7 +105,8 @@ class _Buffers:
         self.tensor = {role: torch.as_tensor(_Raw(ptr, roles[role]), device=device) for role, ptr in self.ptr.items()}
         self.recv = [torch.empty(self.shape, dtype=dt, device=device) for dt in self.dtypes]
         self.flag = torch.zeros(1, dtype=torch.int32, device=device)
-        self.copy_stream = torch.cuda.Stream(device)
+        # one copy stream per source rank, so the copy engines move the chunks concurrently
+        self.copy_streams = [torch.cuda.Stream(device) for _ in range(P)]
         self.calls = 0
 
     def view(self, role: str, dtype) -> torch.Tensor:
@@ -150,7 +151,7 @@ def ulysses_attention_peer(q, k, v, group=None, scale=None, pv_dtype=torch.float
     bufs.calls += 1
     ls2 = (scale if scale is not None else 1.0 / math.sqrt(D)) * LOG2E
     compute = torch.cuda.current_stream(dev)
-    copy = bufs.copy_stream
+    copies = bufs.copy_streams
 
     # 1-2: global per-(b,h) scales, quantisation into the exported send set s
     xs = (q, k, v)
@@ -161,24 +162,22 @@ def ulysses_attention_peer(q, k, v, group=None, scale=None, pv_dtype=torch.float
         ops.quantize_bh(x, scales[i], out_dtype=dt, groups=P, out=bufs.view(f"in{s}_{i}", dt))
     # 3: barrier A
     dist.all_reduce(bufs.flag, group=group)
-    # 4: pull chunk r of every rank's send set (copy engines)
-    copy.wait_stream(compute)
+    # 4: pull chunk r of every rank's send set (copy engines, one stream per source rank)
     chunk = B * S_l * Hl * D
-    for i, dt in enumerate(bufs.dtypes):
-        es = torch.empty((), dtype=dt).element_size()
-        dst = bufs.recv[i]
-        for p in range(P):
+    for p, cs in enumerate(copies):
+        cs.wait_stream(compute)
+        for i, dt in enumerate(bufs.dtypes):
+            es = torch.empty((), dtype=dt).element_size()
             src = bufs.peer[f"in{s}_{i}"][p] + r * chunk * es
-            _copy(dst.data_ptr() + p * chunk * es, Hl * D * es, src, Hl * D * es, Hl * D * es, B * S_l, copy)
-    pulled = torch.cuda.Event()
-    pulled.record(copy)
+            _copy(bufs.recv[i].data_ptr() + p * chunk * es, Hl * D * es, src, Hl * D * es, Hl * D * es, B * S_l, cs)
     cross = None
     if cross_kv is not None:
         from .kernels.fp8_attention import fp8_attention
 
         kt, vt = cross_kv
         cross = fp8_attention(q.transpose(1, 2), kt, vt, scale=scale).transpose(1, 2)
-    compute.wait_event(pulled)
+    for cs in copies:
+        compute.wait_stream(cs)
     # 5: attention over the local heads, into the exported output buffer
     mine = slice(r * Hl, (r + 1) * Hl)
     sq, sk, sv = (sc[:, mine].contiguous()[..., None] for sc in scales)
@@ -196,12 +195,12 @@ def ulysses_attention_peer(q, k, v, group=None, scale=None, pv_dtype=torch.float
     # 6: barrier B
     dist.all_reduce(bufs.flag, group=group)
     # 7: pull chunk r of every rank's output straight into this rank's heads of out
-    copy.wait_stream(compute)
     es = q.element_size()
     row = Hl * D * es
-    for p in range(P):
+    for p, cs in enumerate(copies):
+        cs.wait_stream(compute)
         src = bufs.peer["out"][p] + r * chunk * es
-        _copy(out.data_ptr() + p * row, H * D * es, src, row, row, B * S_l, copy)
-    compute.wait_stream(copy)
-    out.record_stream(copy)
+        _copy(out.data_ptr() + p * row, H * D * es, src, row, row, B * S_l, cs)
+    for cs in copies:
+        compute.wait_stream(cs)
     return out if cross_kv is None else (out, cross)
