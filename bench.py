@@ -17,10 +17,13 @@ stages overlapping on separate streams.
 
 N>1 (torchrun): benchmark configuration 5, the sharded configuration - S=75600 H=40
 D=128 self-attention with Ulysses head parallelism (per-(b,h) scales
-all-reduced, e4m3 q/k and f16 v all-to-all over NCCL, local FP8 attention
-over H/N heads, bf16 all-to-all back), then cross-attention of the local
-query shard to 512 replicated text tokens.  ``value`` = total FLOPs of both
-attentions / max-over-ranks device time ("strong" scaling: total work fixed).
+all-reduced, e4m3 q/k and f16 v exchanged, local FP8 attention over H/N
+heads, bf16 back) plus cross-attention of the local query shard to 512
+replicated text tokens, issued while the input exchange runs.  The exchange
+is copy-engine pulls from the peers' buffers mapped through CUDA IPC
+(``--exchange peer``, default) or NCCL all-to-alls (``--exchange nccl``).
+``value`` = total FLOPs of both attentions / max-over-ranks device time
+("strong" scaling: total work fixed).
 
 The N=1 line also carries, measured after its timed regions on the same
 box: ``competitor_same_box`` - the reference's own Triton attention
@@ -1018,8 +1021,9 @@ def main():
                     help="PV product operands: f16 P/V (default, meets the tolerance) or e4m3")
     ap.add_argument("--linear-rows", type=int, default=32760,
                     help="linear workload: token rows M (32760 = config 4; smaller for ncu captures)")
-    ap.add_argument("--exchange", default="nccl", choices=["nccl", "peer"],
-                    help="N>1: Ulysses exchange by NCCL all-to-alls or by copy-engine pulls from peer buffers")
+    ap.add_argument("--exchange", default="peer", choices=["nccl", "peer"],
+                    help="N>1: Ulysses exchange by copy-engine pulls from peer buffers (CUDA IPC) or by NCCL "
+                         "all-to-alls")
     ap.add_argument("--head-groups", type=int, default=1,
                     help="N>1: head groups of the device-resident Ulysses pipeline (the value line)")
     ap.add_argument("--host-head-groups", type=int, default=0,
