@@ -81,35 +81,53 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled during the timed region.
+
+    Samples every ``period_ms``; ``__enter__`` returns once the first sample
+    has arrived, so sampling covers the whole region even when it is short
+    (that first sample is taken just before the region starts)."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, period_ms: int = 50):
         self.index = index
+        self.period_ms = period_ms
         self.proc = None
+        self.lines = []
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            if ln.strip():
+                self.lines.append(ln)
+                self._first.set()
 
     def __enter__(self):
+        import threading
+
+        self.lines = []
+        self._first = threading.Event()
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", str(self.period_ms)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._reader = threading.Thread(target=self._read, daemon=True)
+            self._reader.start()
+            # sampling is running before the timed region starts (nvidia-smi takes a while to come up)
+            self._first.wait(timeout=5.0)
         except Exception:
             self.proc = None
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-                out = ""
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+            self._reader.join(timeout=5)
 
     def summary(self):
         sm, smax, reasons = [], None, set()
