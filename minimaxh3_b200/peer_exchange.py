@@ -122,12 +122,15 @@ class _Buffers:
 
 
 def ulysses_attention_peer(q, k, v, group=None, scale=None, pv_dtype=torch.float16, out=None, cross_kv=None,
-                           events=None):
+                           events=None, packing=None):
     """``ulysses_attention`` with the exchanges done by copy-engine pulls from peer buffers.
 
     Shards ``[1, S_local, H, D]`` (batch 1), one head group; same arguments
     and result as ``ulysses_attention`` (bit for bit: the same scales, bytes
-    and kernel).  Every rank of ``group`` must be a process on this node.
+    and kernel).  ``packing``: the ``ulysses._Packing`` of a packed batch
+    (per-(sequence, head) scales, the varlen kernel over the global
+    ``cu_seqlens``, rows outside every sequence zero).  Every rank of
+    ``group`` must be a process on this node.
     """
     from . import ops
 
@@ -155,11 +158,18 @@ def ulysses_attention_peer(q, k, v, group=None, scale=None, pv_dtype=torch.float
 
     # 1-2: global per-(b,h) scales, quantisation into the exported send set s
     xs = (q, k, v)
-    amax = torch.stack([ops.absmax_bh(x) for x in xs])                      # [3, B, H]
+    if packing is None:
+        amax = torch.stack([ops.absmax_bh(x) for x in xs])                  # [3, B, H]
+    else:
+        amax = torch.stack([ops.absmax_seg(x, packing.seg) for x in xs])   # [3, nseq, H]
     dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=group)
     scales = ops.scale_from_absmax(amax)
     for i, (x, dt) in enumerate(zip(xs, bufs.dtypes)):
-        ops.quantize_bh(x, scales[i], out_dtype=dt, groups=P, out=bufs.view(f"in{s}_{i}", dt))
+        dst = bufs.view(f"in{s}_{i}", dt)
+        if packing is None:
+            ops.quantize_bh(x, scales[i], out_dtype=dt, groups=P, out=dst)
+        else:
+            ops.quantize_seg(x, packing.seg, scales[i], out_dtype=dt, groups=P, out=dst)
     # 3: barrier A
     dist.all_reduce(bufs.flag, group=group)
     # 4: pull chunk r of every rank's send set (copy engines, one stream per source rank)
@@ -187,8 +197,16 @@ def ulysses_attention_peer(q, k, v, group=None, scale=None, pv_dtype=torch.float
     if events is not None:
         ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
         ev[0].record(compute)
-    ops.attention_e4m3(hq, hk, hv, sq, sk, sv, logit_scale_log2=ls2, out_dtype=q.dtype,
-                       out=send_o.view(P * S_l, Hl, D).permute(1, 0, 2).unsqueeze(0))
+    if packing is None:
+        ops.attention_e4m3(hq, hk, hv, sq, sk, sv, logit_scale_log2=ls2, out_dtype=q.dtype,
+                           out=send_o.view(P * S_l, Hl, D).permute(1, 0, 2).unsqueeze(0))
+    else:
+        # the received buffers are the packed [S, Hl, D] layout in global token order
+        o_rows = send_o.view(P * S_l, Hl, D)
+        ops.attention_e4m3(*(t.view(P * S_l, Hl, D) for t in bufs.recv), sq, sk, sv, logit_scale_log2=ls2,
+                           out_dtype=q.dtype, cu_seqlens_q=packing.cu, cu_seqlens_k=packing.cu,
+                           max_seqlen_q=packing.max_seqlen, out=o_rows)
+        packing.clear_outside(o_rows)
     if ev is not None:
         ev[1].record(compute)
         events.append(ev)

@@ -340,8 +340,8 @@ def ulysses_attention(q, k, v, group=None, scale=None, pv_dtype=torch.float16, a
     view of a ``[B, H, S_local, D]``-strided tensor).
     ``exchange``: ``"nccl"`` (NCCL all-to-alls) or ``"peer"`` (copy-engine
     pulls from the peers' buffers mapped through CUDA IPC,
-    ``peer_exchange.ulysses_attention_peer``: batch 1, one head group, no
-    ``cu_seqlens``, the CUDA kernels; same result bit for bit).
+    ``peer_exchange.ulysses_attention_peer``: batch 1, one head group, the
+    CUDA kernels, with or without ``cu_seqlens``; same result bit for bit).
     ``cu_seqlens``: global offsets (host ints: a list or a CPU tensor, the same
     on every rank) of sequences packed along S of a batch-1 input; attention
     then stays inside each sequence, with per-(sequence, head) scales.
@@ -354,12 +354,16 @@ def ulysses_attention(q, k, v, group=None, scale=None, pv_dtype=torch.float16, a
     batch).
     """
     if exchange == "peer":
-        if head_groups != 1 or cu_seqlens is not None or attn_fn or absmax_fn or quant_fn:
-            raise ValueError("exchange='peer' takes one head group, no cu_seqlens and the CUDA kernels")
+        if head_groups != 1 or attn_fn or absmax_fn or quant_fn:
+            raise ValueError("exchange='peer' takes one head group and the CUDA kernels")
+        if cu_seqlens is not None and cross_kv is not None:
+            raise ValueError("cross_kv is not supported with cu_seqlens")
         from .peer_exchange import ulysses_attention_peer
 
+        P, r = _world(group)
+        packing = _packing(cu_seqlens, P, r, q.shape[0], q.shape[1], q.device)
         return ulysses_attention_peer(q, k, v, group=group, scale=scale, pv_dtype=pv_dtype, out=out,
-                                      cross_kv=cross_kv, events=events)
+                                      cross_kv=cross_kv, events=events, packing=packing)
     if exchange != "nccl":
         raise ValueError("exchange must be 'nccl' or 'peer'")
     P, r = _world(group)

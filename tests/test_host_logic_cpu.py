@@ -65,4 +65,4 @@ def test_ulysses_exchange_argument_is_checked_before_any_collective():
     with pytest.raises(ValueError):
         ulysses_attention(x, x, x, exchange="peer", head_groups=2)
     with pytest.raises(ValueError):
-        ulysses_attention(x, x, x, exchange="peer", cu_seqlens=[0, 8])
+        ulysses_attention(x, x, x, exchange="peer", cu_seqlens=[0, 8], cross_kv=(x, x))

@@ -69,6 +69,7 @@ def _worker(rank, world, port, shape, out_dir):
         shard = [t[:, sl].contiguous() for t in (q, k, v)]
         outs = {G: ulysses_attention(*shard, head_groups=G) for G in (1, 2, 4)}
         packed = {G: ulysses_attention(*shard, head_groups=G, cu_seqlens=PACKED_CU) for G in (1, 2)}
+        packed_peer = [ulysses_attention(*shard, cu_seqlens=PACKED_CU, exchange="peer") for _ in range(2)]
         # host-resident shards, with the cross-attention to replicated text K/V per head group
         gt = torch.Generator().manual_seed(11)
         kt, vt = (torch.randn(B, H, 256, D, generator=gt).to(torch.bfloat16).cuda() for _ in range(2))
@@ -85,7 +86,7 @@ def _worker(rank, world, port, shape, out_dir):
         torch.save({"out": {G: o.cpu() for G, o in outs.items()}, "host": ho.clone(), "host_cross": hc.clone(),
                     "cross": cross.cpu(), "packed": {G: o.cpu() for G, o in packed.items()},
                     "host_packed": hp.clone(), "dev_cross": (dev_o.cpu(), dev_c.cpu()),
-                    "peer": [(o.cpu(), c.cpu()) for o, c in peer]},
+                    "peer": [(o.cpu(), c.cpu()) for o, c in peer], "packed_peer": [o.cpu() for o in packed_peer]},
                    os.path.join(out_dir, f"out{rank}.pt"))
         dist.barrier()
     finally:
@@ -135,6 +136,8 @@ def test_ulysses_two_gpus_bit_identical(tmp_path):
     for G in (1, 2):
         assert torch.equal(torch.cat([x["packed"][G] for x in res], dim=1), packed_ref)
     assert torch.equal(torch.cat([x["host_packed"] for x in res], dim=1), packed_ref)
+    for i in range(2):                                       # copy-engine exchange, packed
+        assert torch.equal(torch.cat([x["packed_peer"][i] for x in res], dim=1), packed_ref)
 
 
 def _single_rank_worker(port, out_dir):
@@ -166,10 +169,12 @@ def _single_rank_worker(port, out_dir):
             res.append((o.clone(), c.clone()))
         cu = [0, 400, 400, 900]                  # an empty sequence; rows 900.. outside every sequence
         packed = ulysses_attention(q, k, v, cu_seqlens=cu)
+        packed_peer = ulysses_attention(q, k, v, cu_seqlens=cu, exchange="peer")
         packed_host = ulysses_attention_host(hq, hk, hv, head_groups=2, cu_seqlens=torch.tensor(cu))
         torch.cuda.synchronize()
         torch.save({"dev": dev_out.cpu(), "cross": cross.cpu(), "host": res, "packed": packed.cpu(),
                     "dev_cross": (dev_o.cpu(), dev_c.cpu()), "peer": [(o.cpu(), c.cpu()) for o, c in peer],
+                    "packed_peer": packed_peer.cpu(),
                     "packed_host": packed_host.clone(), "packed_ref": _packed_single_gpu(q, k, v, cu).cpu()},
                    os.path.join(out_dir, "single.pt"))
     finally:
@@ -193,5 +198,6 @@ def test_host_resident_pipeline_on_one_rank(tmp_path):
     for o, c in r["peer"]:
         assert torch.equal(o, r["dev"]) and torch.equal(c, r["cross"])
     assert torch.equal(r["packed"], r["packed_ref"])          # Ulysses with cu_seqlens = the drop-in varlen path
+    assert torch.equal(r["packed_peer"], r["packed_ref"])
     assert torch.equal(r["packed_host"], r["packed_ref"])
     assert torch.count_nonzero(r["packed"][0, 900:]) == 0
