@@ -114,7 +114,8 @@ class _Buffers:
 
     @classmethod
     def get(cls, group, device, B, S_l, Hl, D, pv_dtype, out_dtype):
-        key = (id(group) if group is not None else None, str(device), B, S_l, Hl, D, pv_dtype, out_dtype)
+        ranks = tuple(dist.get_process_group_ranks(group if group is not None else dist.group.WORLD))
+        key = (ranks, str(device), B, S_l, Hl, D, pv_dtype, out_dtype)
         ent = cls._cache.get(key)
         if ent is None:
             ent = cls._cache[key] = cls(group, device, B, S_l, Hl, D, pv_dtype, out_dtype)
