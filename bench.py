@@ -477,6 +477,15 @@ def run_ulysses_arm(args, dist, rank, world, local):
     t = torch.tensor([e0.elapsed_time(e1)], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t[0])
+    # Check after the timed regions: one step through each exchange must give the same bits on
+    # every rank (the copy-engine pulls against NCCL's all-to-alls), reduced over the ranks.
+    o_peer, c_peer = ulysses_attention(q, k, v, head_groups=1, cross_kv=(kt, vt), exchange="peer")
+    o_nccl, c_nccl = ulysses_attention(q, k, v, head_groups=1, cross_kv=(kt, vt), exchange="nccl")
+    same = torch.tensor([1 if torch.equal(o_peer, o_nccl) and torch.equal(c_peer, c_nccl) else 0],
+                        device=dev, dtype=torch.int32)
+    dist.all_reduce(same, op=dist.ReduceOp.MIN)
+    exchange_check = {"peer_equals_nccl_bitwise": bool(int(same.item())), "ranks": world}
+    del o_peer, c_peer, o_nccl, c_nccl
     if rank != 0:
         return
     # The same workload on rank 0's GPU alone (no collectives), so the sharded value can be
@@ -509,6 +518,7 @@ def run_ulysses_arm(args, dist, rank, world, local):
         # per step: the cross-attention's 5 quantisation kernels + 1 attention
         "gpu_launches": (7 * G + 6) * args.steps, "clocks": clk.summary(),
         "n1_same_workload": n1,
+        "exchange_check": exchange_check,
     }
     print(json.dumps(line), flush=True)
 
