@@ -85,15 +85,19 @@ class ClockSampler:
 
     Samples every ``period_ms``; ``__enter__`` returns once the first sample
     has arrived, so sampling covers the whole region even when it is short
-    (that first sample is taken just before the region starts)."""
+    (that first sample is taken just before the region starts).  Enter it
+    before the barrier that starts the timed region: the wait for the first
+    sample differs between processes.  ``enabled=False`` (ranks whose clocks
+    are not reported) samples nothing."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int, period_ms: int = 50):
+    def __init__(self, index: int, period_ms: int = 50, enabled: bool = True):
         self.index = index
         self.period_ms = period_ms
+        self.enabled = enabled
         self.proc = None
         self.lines = []
 
@@ -108,6 +112,8 @@ class ClockSampler:
 
         self.lines = []
         self._first = threading.Event()
+        if not self.enabled:
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
@@ -435,12 +441,12 @@ def run_ulysses_arm(args, dist, rank, world, local):
 
     for _ in range(args.warmup):
         step()
-    torch.cuda.synchronize(dev)
-    dist.barrier()
-    torch.cuda.synchronize(dev)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(local, args.clock_period_ms, enabled=rank == 0) as clk:
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        torch.cuda.synchronize(dev)
         t0.record(stream)
         for i in range(args.steps):
             step(attn_ev)
@@ -557,13 +563,13 @@ def run_gpu_arm(args, dist, rank, world, local):
 
     for _ in range(args.warmup):
         step()
-    torch.cuda.synchronize(dev)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    with ClockSampler(local) as clk:
+    with ClockSampler(local, args.clock_period_ms, enabled=rank == 0) as clk:
+        torch.cuda.synchronize(dev)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
         t_start.record(stream)
@@ -1049,6 +1055,8 @@ def main():
                     help="PV product operands: f16 P/V (default, meets the tolerance) or e4m3")
     ap.add_argument("--linear-rows", type=int, default=32760,
                     help="linear workload: token rows M (32760 = config 4; smaller for ncu captures)")
+    ap.add_argument("--clock-period-ms", type=int, default=50,
+                    help="nvidia-smi clock sampling period during the timed region")
     ap.add_argument("--exchange", default="peer", choices=["nccl", "peer"],
                     help="N>1: Ulysses exchange by copy-engine pulls from peer buffers (CUDA IPC) or by NCCL "
                          "all-to-alls")
