@@ -37,8 +37,9 @@ extern "C" {
  * mh3_quantize_bh, mh3_copy_rows, mh3_step_diff; 4: f32 input to
  * mh3_quantize_rows, test_flags in mh3_attn_args (was reserved0) and
  * mh3_gemm_args; 5: mh3_absmax_seg, mh3_quantize_seg; 6: mh3_peer_alloc,
- * mh3_peer_free, mh3_peer_handle, mh3_peer_open, mh3_peer_close. */
-#define MH3_ABI_VERSION 6
+ * mh3_peer_free, mh3_peer_handle, mh3_peer_open, mh3_peer_close;
+ * 7: mh3_key_bias. */
+#define MH3_ABI_VERSION 7
 
 #define MH3_OK 0
 #define MH3_ERR_INVALID (-1)     /* bad argument: shape, stride, alignment, null pointer */
@@ -136,6 +137,26 @@ typedef struct mh3_attn_args {
 } mh3_attn_args;
 
 MH3_API int mh3_fp8_attention_fwd(const mh3_attn_args* args, void* stream);
+
+/*
+ * The per-key inputs of the drop-in path in the form mh3_fp8_attention_fwd
+ * takes (key_bias2 and kv_len), in one launch.  Replaces the reference's
+ * in-kernel handling of ``key_bias`` / ``key_mask``
+ * (kernels/fp8_attention.py:256-264): key j of batch b is valid when
+ * key_mask[b,j] != 0 and key_bias[b,j] > -1e8;
+ *   bias2[b,j] = key_bias[b,j] * 1.4426950408889634f (fp32 product; 0 with no
+ *                bias) for a valid key, -inf for an invalid one and for
+ *                j in [seqlen_k, ceil(seqlen_k/128)*128);
+ *   kv_len[b]  = one past the last valid key (0 when none is).
+ * key_mask: uint8 (bool) [batch, seqlen_k], keys contiguous, batch stride
+ * mask_stride_b elements (0 = one row for every batch), or NULL.  key_bias:
+ * f32, the same layout with bias_stride_b, or NULL.  bias2: f32 rows of
+ * bias2_stride_b >= ceil(seqlen_k/128)*128.  kv_len: int32 [batch] or NULL.
+ * (ABI version 7.)
+ */
+MH3_API int mh3_key_bias(const uint8_t* key_mask, int64_t mask_stride_b, const float* key_bias, int64_t bias_stride_b,
+                         int64_t batch, int64_t seqlen_k, float* bias2, int64_t bias2_stride_b, int32_t* kv_len,
+                         void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Q / K / V quantisation for the drop-in bf16/fp16 path                      */

@@ -90,6 +90,7 @@ _SIGNATURES = {
     "mh3_last_error": (ctypes.c_char_p, []),
     "mh3_device_error_word": (c_ptr, []),
     "mh3_fp8_attention_fwd": (c_i32, [ctypes.POINTER(AttnArgs), c_ptr]),
+    "mh3_key_bias": (c_i32, [c_ptr, c_i64, c_ptr, c_i64, c_i64, c_i64, c_ptr, c_i64, c_ptr, c_ptr]),
     "mh3_qkv_workspace_bytes": (c_u64, [c_i32, c_i32, c_i32, c_i32]),
     "mh3_quantize_qkv": (c_i32, [ctypes.POINTER(QkvQuantArgs), c_ptr]),
     "mh3_quantize_qkv_noalloc": (c_i32, [ctypes.POINTER(QkvQuantArgs), c_ptr]),

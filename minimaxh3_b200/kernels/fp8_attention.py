@@ -97,9 +97,8 @@ def _fp8_attention_impl(q, k, v, scale, key_mask, key_bias, repair_tau):
     q8, k8, v8, sq, sk, sv, _ = _ops.quantize_qkv(q, k, v, c, v_dtype=_pv_dtype())
     bias2 = kv_len = None
     if key_mask is not None or key_bias is not None:
-        bias2 = _ops.build_key_bias2(key_mask, key_bias, B, Sk, q.device)
-        # padded batches: the tiles past each batch's last valid key are skipped
-        kv_len = _ops.key_valid_len(key_mask, key_bias, B, Sk, q.device)
+        # one launch; padded batches: the tiles past each batch's last valid key are skipped
+        bias2, kv_len = _ops.key_bias_inputs(key_mask, key_bias, B, Sk, q.device)
     # Same strides as the reference's ``torch.empty_like(q)`` (:379); the
     # kernel writes through the strides, so transposed views stay correct.
     out = torch.empty_like(q)

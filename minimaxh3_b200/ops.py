@@ -9,7 +9,6 @@ these paths.
 from __future__ import annotations
 
 import collections
-import math
 
 import torch
 
@@ -209,39 +208,43 @@ def attention_e4m3(
     return out
 
 
-def key_valid_len(key_mask, key_bias, B: int, Sk: int, device) -> torch.Tensor:
-    """int32 [B]: one past the last key that the mask / bias leaves valid
-    (0 when none is), computed on the device without a host sync.  Keys at
-    or past it are masked, so the kernel may skip their tiles (``kv_len``);
-    a padded batch then costs only its real keys."""
-    valid = torch.ones((B, Sk), dtype=torch.bool, device=device)
-    if key_bias is not None:
-        valid = valid & (key_bias.to(device=device, dtype=torch.float32).expand(B, Sk) > -1.0e8)
+def _per_key_rows(t, B: int, Sk: int, dtype, device, what: str):
+    """A per-key input as (tensor with contiguous keys, batch stride): shapes
+    [Sk], [1, Sk] (one row for every batch, stride 0) or [B, Sk]."""
+    t = t.to(device=device, dtype=dtype)
+    if t.dim() == 1:
+        t = t.unsqueeze(0)
+    if t.dim() != 2 or t.shape[1] != Sk or t.shape[0] not in (1, B):
+        raise ValueError(f"{what} must be [B, Sk], [1, Sk] or [Sk] with Sk = {Sk}")
+    if t.stride(1) != 1:
+        t = t.contiguous()
+    return t, (t.stride(0) if t.shape[0] == B and B > 1 else 0)
+
+
+def key_bias_inputs(key_mask, key_bias, B: int, Sk: int, device):
+    """The drop-in path's per-key inputs in the attention kernel's form, one
+    launch (``mh3_key_bias``): ``(bias2, kv_len)`` with bias2 an fp32
+    ``[B, ceil(Sk/128)*128]`` additive log2 bias (``key_bias * log2(e)`` for a
+    valid key, ``-inf`` for a masked one and for the padding; the reference's
+    rule, fp8_attention.py:256-264: a key is valid when its mask is true and
+    its bias is above -1e8) and kv_len an int32 ``[B]``, one past the last
+    valid key, past which the kernel skips whole tiles."""
+    lib = _lib.load()
+    mask_ptr = bias_ptr = 0
+    msb = bsb = 0
     if key_mask is not None:
-        valid = valid & key_mask.to(device=device, dtype=torch.bool).expand(B, Sk)
-    idx = torch.arange(1, Sk + 1, dtype=torch.int32, device=device)
-    return torch.where(valid, idx, torch.zeros_like(idx)).amax(dim=1).to(torch.int32)
-
-
-def build_key_bias2(key_mask, key_bias, B: int, Sk: int, device) -> torch.Tensor:
-    """Per-key additive bias in log2 units, [B, ceil(Sk/128)*128], -inf = masked.
-
-    Folds the reference's two per-key inputs (fp8_attention.py:256-264):
-    ``key_bias`` adds ``bias * log2(e)`` and a bias <= -1e8 masks the key;
-    ``key_mask`` False masks the key.  The padding past Sk is masked too.
-    """
-    nk = _cdiv(Sk, BLOCK)
-    buf = torch.full((B, nk * BLOCK), -math.inf, dtype=torch.float32, device=device)
-    val = torch.zeros((B, Sk), dtype=torch.float32, device=device)
-    valid = torch.ones((B, Sk), dtype=torch.bool, device=device)
+        m, msb = _per_key_rows(key_mask, B, Sk, torch.bool, device, "key_mask")
+        mask_ptr = m.data_ptr()
     if key_bias is not None:
-        kb = key_bias.to(device=device, dtype=torch.float32).expand(B, Sk)
-        valid = valid & (kb > -1.0e8)
-        val = kb * torch.tensor(LOG2E, dtype=torch.float32, device=device)
-    if key_mask is not None:
-        valid = valid & key_mask.to(device=device, dtype=torch.bool).expand(B, Sk)
-    buf[:, :Sk] = torch.where(valid, val, torch.full_like(val, -math.inf))
-    return buf
+        kb, bsb = _per_key_rows(key_bias, B, Sk, torch.float32, device, "key_bias")
+        bias_ptr = kb.data_ptr()
+    bias2 = torch.empty((B, _cdiv(Sk, BLOCK) * BLOCK), dtype=torch.float32, device=device)
+    kv_len = torch.empty((B,), dtype=torch.int32, device=device)
+    with torch.cuda.device(bias2.device):
+        rc = lib.mh3_key_bias(mask_ptr or None, msb, bias_ptr or None, bsb, B, Sk, bias2.data_ptr(),
+                              bias2.stride(0), kv_len.data_ptr(), _stream(bias2.device))
+    _lib.check(rc, "mh3_key_bias")
+    return bias2, kv_len
 
 
 # ---------------------------------------------------------------------------

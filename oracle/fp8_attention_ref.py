@@ -192,6 +192,32 @@ def attention_kernel_ref(
     return out.to(out_dtype)                                       # :296-297, :403
 
 
+def key_bias2_ref(key_mask, key_bias, B: int, Sk: int, tile: int = 128):
+    """The reference's per-key validity and bias (fp8_attention.py:256-262) in
+    the form the CUDA kernel takes: ``(bias2, kv_len)``.
+
+    A key is valid when ``key_mask`` is true and ``key_bias > -1e8``;
+    ``bias2[b, j] = fp32(key_bias * fp32(log2 e))`` for a valid key (0 with no
+    bias), ``-inf`` for an invalid key and for the padding up to a whole
+    ``tile``; ``kv_len[b]`` is one past the last valid key (0 if none).
+    ``key_mask`` / ``key_bias`` broadcast over the batch ([Sk], [1, Sk] or
+    [B, Sk]).  CPU tensors in, CPU tensors out.
+    """
+    valid = torch.ones((B, Sk), dtype=torch.bool)
+    val = torch.zeros((B, Sk), dtype=torch.float32)
+    if key_bias is not None:
+        kb = key_bias.cpu().float().reshape(-1, Sk).expand(B, Sk)
+        valid = valid & (kb > -1.0e8)                          # :258
+        val = kb * _f32(LOG2E)                                 # :259
+    if key_mask is not None:
+        valid = valid & key_mask.cpu().bool().reshape(-1, Sk).expand(B, Sk)   # :261-262
+    bias2 = torch.full((B, cdiv(Sk, tile) * tile), -math.inf, dtype=torch.float32)
+    bias2[:, :Sk] = torch.where(valid, val, torch.full_like(val, -math.inf))
+    idx = torch.arange(1, Sk + 1, dtype=torch.int32)
+    kv_len = torch.where(valid, idx, torch.zeros_like(idx)).amax(dim=1).to(torch.int32)
+    return bias2, kv_len
+
+
 def fp8_attention_ref(
     q: torch.Tensor,
     k: torch.Tensor,

@@ -35,7 +35,7 @@ def test_binding_covers_header():
 
 def test_host_only_calls():
     lib = _lib.load()
-    assert lib.mh3_abi_version() == 6
+    assert lib.mh3_abi_version() == 7
     assert lib.mh3_qkv_workspace_bytes(1, 40, 32760, 128) == 2 * 40 * 128 * 128 * 4
     assert lib.mh3_qkv_workspace_bytes(0, 1, 1, 128) == 0
 
@@ -54,6 +54,11 @@ def test_invalid_arguments_are_rejected_without_gpu():
     q.head_dim = 128
     assert lib.mh3_quantize_qkv(q, None) == _lib.MH3_ERR_INVALID
     assert lib.mh3_quantize_rows(None, 8, 0, 4, 12, None, None, None) == _lib.MH3_ERR_INVALID
+    # mh3_key_bias: null output, empty sizes, rows shorter than a whole 128-key tile
+    assert lib.mh3_key_bias(None, 0, None, 0, 2, 300, None, 384, None, None) == _lib.MH3_ERR_INVALID
+    assert lib.mh3_key_bias(None, 0, None, 0, 0, 300, 16, 384, None, None) == _lib.MH3_ERR_INVALID
+    assert lib.mh3_key_bias(None, 0, None, 0, 2, 300, 16, 300, None, None) == _lib.MH3_ERR_INVALID
+    assert b"ceil(seqlen_k/128)*128" in lib.mh3_last_error()
 
 
 def test_struct_sizes_match_c_layout():

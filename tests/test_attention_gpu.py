@@ -117,7 +117,7 @@ def test_attention_key_bias_and_mask(pv):
     key_mask = torch.rand(B, Sk, generator=g) > 0.2
     key_mask[1, :] = False  # a batch with every key masked -> zeros
     ls2 = OA.LOG2E / math.sqrt(D)
-    bias2 = ops.build_key_bias2(key_mask.to(DEV), key_bias.to(DEV), B, Sk, DEV)
+    bias2, _ = ops.key_bias_inputs(key_mask.to(DEV), key_bias.to(DEV), B, Sk, DEV)
     out = _run_e4m3(q8, k8, v8, sq[..., None], sk[..., None], sv[..., None], ls2, pv=pv,
                     key_bias2=bias2).float().cpu()
     ref = OA.sdpa_dequant_oracle(q8.double() * sq[..., None, None], k8.double() * sk[..., None, None],
@@ -215,7 +215,7 @@ def test_attention_rising_row_max(pv, use_bias):
     ls2 = OA.LOG2E / math.sqrt(D)
     kw = {}
     if use_bias:
-        kw["key_bias2"] = ops.build_key_bias2(None, key_bias.to(DEV), B, Sk, DEV)
+        kw["key_bias2"], _ = ops.key_bias_inputs(None, key_bias.to(DEV), B, Sk, DEV)
     out = _run_e4m3(q8, k8, v8, sq[..., None], sk[..., None], sv[..., None], ls2, pv=pv, **kw).float().cpu()
     assert torch.isfinite(out).all()
     ref = OA.sdpa_dequant_oracle(q8.double() * sq[..., None, None], k8.double() * sk[..., None, None],
@@ -274,12 +274,11 @@ def test_padded_batch_kv_len_skips_tiles_exactly(pv):
     key_mask = torch.arange(Sk)[None, :] < lens[:, None]
     out = fp8_attention(q.to(DEV), k.to(DEV), v.to(DEV), key_mask=key_mask.to(DEV)).float().cpu()
     assert torch.isfinite(out).all()
-    kv = ops.key_valid_len(key_mask.to(DEV), None, B, Sk, DEV)
+    bias2, kv = ops.key_bias_inputs(key_mask.to(DEV), None, B, Sk, DEV)
     assert kv.cpu().tolist() == lens.tolist()
     # same bytes through the kernel with and without the per-batch length
     (q8, sq), (k8, sk), (v8, sv) = _per_bh(q), _per_bh(k), _per_bh(v)
     ls2 = OA.LOG2E / math.sqrt(D)
-    bias2 = ops.build_key_bias2(key_mask.to(DEV), None, B, Sk, DEV)
     args = (q8, k8, v8, sq[..., None], sk[..., None], sv[..., None], ls2)
     full = _run_e4m3(*args, pv=pv, key_bias2=bias2)
     skip = _run_e4m3(*args, pv=pv, key_bias2=bias2, kv_len=kv)
