@@ -1003,8 +1003,8 @@ def run_step_workload(args):
     """Step-residual cache reductions (runtime/step_cache.py:39-52; not the headline).
 
     The per-step relative change of block 0's output plus the copy of it kept
-    for the next step, on a bf16 hidden state [1, 75600, 5120] (config 5's
-    tokens x the DiT width, 774 MB): ``ops.step_diff(copy=True)`` against the
+    for the next step, on a bf16 hidden state [1, T, 5120] (``--step-tokens``
+    T, by default config 5's 75600 tokens x the DiT width, 774 MB): ``ops.step_diff(copy=True)`` against the
     reference's arithmetic (two fp32 copies, a difference, two abs, two means,
     ``.item()``, clone).  Algorithmic bytes: h1 and h1_prev read once, h1_prev
     written once.
@@ -1014,8 +1014,9 @@ def run_step_workload(args):
     dev = torch.device("cuda", 0)
     stream = torch.cuda.current_stream(dev)
     g = torch.Generator(device=dev).manual_seed(0)
-    h1 = torch.randn(1, 75600, 5120, generator=g, device=dev).to(torch.bfloat16)
-    prev = (h1.float() + 0.01 * torch.randn(1, 75600, 5120, generator=g, device=dev)).to(torch.bfloat16)
+    T = args.step_tokens
+    h1 = torch.randn(1, T, 5120, generator=g, device=dev).to(torch.bfloat16)
+    prev = (h1.float() + 0.01 * torch.randn(1, T, 5120, generator=g, device=dev)).to(torch.bfloat16)
     peaks = _peaks()
 
     def fused():
@@ -1032,7 +1033,7 @@ def run_step_workload(args):
     ms = _time_cuda(fused, args.steps, args.warmup, stream)
     ms_ref = _time_cuda(reference, args.steps, args.warmup, stream)
     algo = 3 * h1.numel() * 2
-    print(json.dumps({"workload": "step cache: relative change + kept copy of a bf16 [1, 75600, 5120] hidden state",
+    print(json.dumps({"workload": f"step cache: relative change + kept copy of a bf16 [1, {T}, 5120] hidden state",
                       "unit": "ms", "fused_ms": ms, "reference_arithmetic_ms": ms_ref, "algorithmic_bytes": algo,
                       "fused_gbs": algo / ms / 1e6, "frac_of_hbm": algo / ms / 1e6 / peaks["hbm_gbs"],
                       "includes": "one device->host read of the sums (the step's host sync)"}), flush=True)
@@ -1055,6 +1056,8 @@ def main():
                     help="PV product operands: f16 P/V (default, meets the tolerance) or e4m3")
     ap.add_argument("--linear-rows", type=int, default=32760,
                     help="linear workload: token rows M (32760 = config 4; smaller for ncu captures)")
+    ap.add_argument("--step-tokens", type=int, default=75600,
+                    help="step workload: hidden-state tokens (75600 = config 5; smaller for ncu captures)")
     ap.add_argument("--clock-period-ms", type=int, default=50,
                     help="nvidia-smi clock sampling period during the timed region")
     ap.add_argument("--exchange", default="peer", choices=["nccl", "peer"],

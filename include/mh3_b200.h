@@ -151,8 +151,9 @@ MH3_API int mh3_fp8_attention_fwd(const mh3_attn_args* args, void* stream);
  * key_mask: uint8 (bool) [batch, seqlen_k], keys contiguous, batch stride
  * mask_stride_b elements (0 = one row for every batch), or NULL.  key_bias:
  * f32, the same layout with bias_stride_b, or NULL.  bias2: f32 rows of
- * bias2_stride_b >= ceil(seqlen_k/128)*128.  kv_len: int32 [batch] or NULL.
- * (ABI version 7.)
+ * bias2_stride_b >= ceil(seqlen_k/128)*128.  kv_len: int32 [batch] or NULL
+ * (zeroed on the stream, then reduced with atomics).  batch <= 65535,
+ * seqlen_k <= 2^30.  (ABI version 7.)
  */
 MH3_API int mh3_key_bias(const uint8_t* key_mask, int64_t mask_stride_b, const float* key_bias, int64_t bias_stride_b,
                          int64_t batch, int64_t seqlen_k, float* bias2, int64_t bias2_stride_b, int32_t* kv_len,
