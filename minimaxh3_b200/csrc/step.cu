@@ -19,6 +19,7 @@ namespace step {
 
 constexpr int kThreads = 256;
 constexpr int kBlocks = 148 * 4;  // fixed grid: the reduction order depends only on n
+constexpr int kUnroll = 4;        // 16-byte vector pairs loaded ahead per thread
 
 template <typename T>
 __device__ __forceinline__ float to_f(T v);
@@ -42,9 +43,8 @@ __global__ void __launch_bounds__(kThreads) diff_kernel(const T* __restrict__ h1
     const long long nvec = (hi - lo) / V;  // lo is a multiple of V (chunk is)
     const uint4* a4 = reinterpret_cast<const uint4*>(h1 + lo);
     uint4* p4 = reinterpret_cast<uint4*>(prev + lo);
-    for (long long i = threadIdx.x; i < nvec; i += kThreads) {
-      const uint4 ua = __ldcs(a4 + i);
-      const uint4 up = __ldcs(p4 + i);
+    // One 16-byte vector pair: per-vector fp32 partials folded into the double sums.
+    auto fold = [&](const uint4& ua, const uint4& up) {
       const T* ea = reinterpret_cast<const T*>(&ua);
       const T* ep = reinterpret_cast<const T*>(&up);
       float fd = 0.0f, fp = 0.0f;
@@ -56,13 +56,36 @@ __global__ void __launch_bounds__(kThreads) diff_kernel(const T* __restrict__ h1
       }
       sd += (double)fd;
       sp += (double)fp;
+    };
+    // kUnroll vectors' loads are issued before any is folded (enough bytes in
+    // flight per SM for HBM); each thread still folds its vectors i,
+    // i + kThreads, i + 2*kThreads, ... in that order, so the sums do not
+    // depend on the unrolling.
+    long long i = threadIdx.x;
+    for (; i + (kUnroll - 1) * kThreads < nvec; i += kUnroll * kThreads) {
+      uint4 ua[kUnroll], up[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        ua[u] = __ldcs(a4 + i + u * kThreads);
+        up[u] = __ldcs(p4 + i + u * kThreads);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        fold(ua[u], up[u]);
+        if (copy) __stcs(p4 + i + u * kThreads, ua[u]);
+      }
+    }
+    for (; i < nvec; i += kThreads) {
+      const uint4 ua = __ldcs(a4 + i);
+      const uint4 up = __ldcs(p4 + i);
+      fold(ua, up);
       if (copy) __stcs(p4 + i, ua);
     }
-    for (long long i = lo + nvec * V + threadIdx.x; i < hi; i += kThreads) {
-      const float x = to_f<T>(h1[i]), y = to_f<T>(prev[i]);
+    for (long long e = lo + nvec * V + threadIdx.x; e < hi; e += kThreads) {  // ragged tail
+      const float x = to_f<T>(h1[e]), y = to_f<T>(prev[e]);
       sd += (double)fabsf(x - y);
       sp += (double)fabsf(y);
-      if (copy) prev[i] = h1[i];
+      if (copy) prev[e] = h1[e];
     }
   }
   __shared__ double rd[kThreads / 32], rp[kThreads / 32];

@@ -6,7 +6,7 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
-@pytest.mark.parametrize("n", [1, 7, 1000, 8 * 592 + 3, 3_000_001])
+@pytest.mark.parametrize("n", [1, 7, 1000, 8 * 592 + 3, 3_000_001, 12_582_917])  # the last: unrolled loads per thread
 def test_step_diff_sums_copy_and_determinism(dtype, n):
     from minimaxh3_b200 import ops
 
