@@ -205,6 +205,33 @@ def _reference_kernels():
     return importlib.import_module("kernels.fp8_attention"), importlib.import_module("kernels.fp8_linear")
 
 
+def _reference_cpu_path():
+    """``(fn, kind, source)``: the reference's CPU path for attention.
+
+    With the unmodified copy in baseline/_ref, the reference's own
+    ``routed_sdpa`` inside its ``denoiser_scope`` (kernels/attention_router.py:
+    56-102,133-139): on CPU tensors ``is_supported`` is false and it takes its
+    torch SDPA fallback (``kind`` "reference").  Without the copy, the
+    oracle's restatement of that fallback (``kind`` "port").
+    """
+    try:
+        _reference_kernels()  # puts baseline/_ref on sys.path (raises without the copy)
+        import importlib
+
+        router = importlib.import_module("kernels.attention_router")
+
+        def fn(q, k, v):
+            with router.denoiser_scope():
+                return router.routed_sdpa(q, k, v)
+
+        return fn, "reference", "baseline/_ref kernels/attention_router.py routed_sdpa (unmodified; CPU tensors " \
+                                "take its torch SDPA fallback)"
+    except Exception:  # noqa: BLE001 - no reference copy, or it does not import here
+        from oracle.router_ref import cpu_sdpa_fallback
+
+        return cpu_sdpa_fallback, "port", "oracle/router_ref.py cpu_sdpa_fallback (attention_router.py:93-102)"
+
+
 def _median_ms(fn, stream, warmup=3, reps=20):
     """The competitor protocol: warm-ups, then the median of CUDA-event timings."""
     for _ in range(warmup):
@@ -291,8 +318,8 @@ def triton_competitor(q, k, v, stream):
 
 
 def cpu_reference_sample(seconds: float = 10.0):
-    """The reference's CPU path (torch SDPA fallback) on a bounded sample of config 2."""
-    from oracle.router_ref import cpu_sdpa_fallback
+    """The reference's CPU path (routed_sdpa -> torch SDPA fallback) on a bounded sample of config 2."""
+    ref_sdpa, kind, source = _reference_cpu_path()
 
     g = torch.Generator().manual_seed(0)
     rows = 512
@@ -301,16 +328,16 @@ def cpu_reference_sample(seconds: float = 10.0):
     v = torch.randn(1, 1, S, D, generator=g)
     flop = 4.0 * rows * S * D
     for _ in range(2):
-        cpu_sdpa_fallback(q, k, v)
+        ref_sdpa(q, k, v)
     n, t0 = 0, time.perf_counter()
     while True:
-        cpu_sdpa_fallback(q, k, v)
+        ref_sdpa(q, k, v)
         n += 1
         el = time.perf_counter() - t0
         if el >= seconds:
             break
     return {"value": flop * n / el / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
-            "kind": "port",
+            "kind": kind, "source": source,
             "sample": f"torch SDPA fp32 on CPU, 1 head x {rows} query rows x {S} keys x D={D}, {n} calls "
                       f"in {el:.1f}s (the reference's routed_sdpa CPU fallback)"}
 
@@ -321,16 +348,16 @@ def cpu_config1():
     import platform
     import statistics
 
-    from oracle.router_ref import cpu_sdpa_fallback
+    ref_sdpa, _, _ = _reference_cpu_path()
 
     g = torch.Generator().manual_seed(0)
     q, k, v = (torch.randn(1, 8, 1024, 128, generator=g) for _ in range(3))
     for _ in range(3):
-        cpu_sdpa_fallback(q, k, v)
+        ref_sdpa(q, k, v)
     ts = []
     for _ in range(20):
         t0 = time.perf_counter()
-        cpu_sdpa_fallback(q, k, v)
+        ref_sdpa(q, k, v)
         ts.append(time.perf_counter() - t0)
     med = statistics.median(ts)
     return {"ms": med * 1e3, "tflops": 4.0 * 8 * 1024 * 1024 * 128 / med / 1e12, "cpu_count": os.cpu_count(),
@@ -341,7 +368,7 @@ def run_reference_arm(args, rank):
     if rank != 0:
         return
     torch.set_num_threads(os.cpu_count() or 1)
-    from oracle.router_ref import cpu_sdpa_fallback
+    ref_sdpa, kind, source = _reference_cpu_path()
 
     g = torch.Generator().manual_seed(0)
     rows = 256
@@ -350,10 +377,10 @@ def run_reference_arm(args, rank):
     v = torch.randn(1, 1, S, D, generator=g)
     flop = 4.0 * rows * S * D
     for _ in range(max(args.warmup, 1)):
-        cpu_sdpa_fallback(q, k, v)
+        ref_sdpa(q, k, v)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        cpu_sdpa_fallback(q, k, v)
+        ref_sdpa(q, k, v)
     el = time.perf_counter() - t0
     val = flop * args.steps / el / 1e12
     line = {"metric": "FP8 attention TFLOPS (S=32760 H=40 D=128)", "value": val, "unit": "TFLOP/s",
@@ -361,7 +388,8 @@ def run_reference_arm(args, rank):
             "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "config2 sample: 1 head x 256 query rows x 32760 keys, D=128, CPU"},
-            "cpu_baseline": {"value": val, "unit": "TFLOP/s", "kind": "port", "cores": torch.get_num_threads(),
+            "cpu_baseline": {"value": val, "unit": "TFLOP/s", "kind": kind, "source": source,
+                             "cores": torch.get_num_threads(),
                              "sample": "torch SDPA fp32 on CPU (routed_sdpa fallback), 1 head x 256 rows x "
                                        "32760 keys per step"},
             "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
