@@ -163,8 +163,23 @@ def _dist():
 
         local = int(os.environ.get("LOCAL_RANK", "0"))
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        # NCCL may print a version banner on stdout when it creates the
+        # communicator (eagerly here: device_id is given); stdout carries only
+        # the result line, so fd 1 points at stderr until the first collective
+        # has run and C-level buffers are flushed.
+        import ctypes
+
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+            dist.barrier()
+        finally:
+            ctypes.CDLL(None).fflush(None)
+            os.dup2(saved, 1)
+            os.close(saved)
         return dist, dist.get_rank(), ws, local
     return None, 0, 1, 0
 
