@@ -566,6 +566,7 @@ static cudaError_t dispatch(const Params& p, dim3 grid, cudaStream_t st, bool f1
 using namespace mh3;
 
 extern "C" int mh3_fp8_attention_fwd(const mh3_attn_args* a, void* stream) {
+  const mh3::NvtxRange nvtx_range("mh3_fp8_attention_fwd");
   if (a == nullptr) return fail(MH3_ERR_INVALID, "mh3_fp8_attention_fwd: null args");
   const int D = a->head_dim;
   if (D != 64 && D != 128) return fail(MH3_ERR_INVALID, "head_dim must be 64 or 128");

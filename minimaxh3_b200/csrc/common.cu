@@ -99,6 +99,7 @@ extern "C" int* mh3_device_error_word(void) { return mh3::device_error_word(); }
 
 extern "C" int mh3_copy_rows(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch, int64_t row_bytes,
                              int64_t rows, void* stream) {
+  const mh3::NvtxRange nvtx_range("mh3_copy_rows");
   if (rows == 0 || row_bytes == 0) return MH3_OK;
   if (dst == nullptr || src == nullptr || rows < 0 || row_bytes < 0 || dst_pitch < row_bytes || src_pitch < row_bytes)
     return mh3::fail(MH3_ERR_INVALID, "mh3_copy_rows: bad pointers, pitches or sizes");

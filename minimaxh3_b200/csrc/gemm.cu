@@ -648,6 +648,7 @@ static cudaError_t launch(const Params& p, cudaStream_t st) {
 using namespace mh3;
 
 extern "C" int mh3_scaled_gemm(const mh3_gemm_args* a, void* stream) {
+  const mh3::NvtxRange nvtx_range("mh3_scaled_gemm");
   if (a == nullptr) return fail(MH3_ERR_INVALID, "mh3_scaled_gemm: null args");
   if (a->M < 0 || a->N <= 0 || a->K <= 0) return fail(MH3_ERR_INVALID, "sizes must be positive");
   if (a->M == 0) return MH3_OK;

@@ -73,6 +73,7 @@ using namespace mh3;
 extern "C" int mh3_key_bias(const uint8_t* key_mask, int64_t mask_stride_b, const float* key_bias,
                             int64_t bias_stride_b, int64_t batch, int64_t seqlen_k, float* bias2,
                             int64_t bias2_stride_b, int32_t* kv_len, void* stream) {
+  const mh3::NvtxRange nvtx_range("mh3_key_bias");
   if (batch <= 0 || seqlen_k <= 0) return fail(MH3_ERR_INVALID, "mh3_key_bias: batch and seqlen_k must be positive");
   if (batch > 65535 || seqlen_k > (1LL << 30))
     return fail(MH3_ERR_INVALID, "mh3_key_bias: batch must be <= 65535 and seqlen_k <= 2^30");

@@ -5,6 +5,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 #include <stdint.h>
 #include <string.h>
 
@@ -31,5 +32,17 @@ int* device_error_word();
 // The calling thread's current CUDA context (CUcontext), or null; through
 // the runtime's driver entry point, so the library does not link libcuda.
 void* current_context();
+
+// NVTX range named after a C entry point, over its host-side work (argument
+// checks and launches), so a profiler can attribute kernels to entry points
+// (e.g. ncu --nvtx --nvtx-include "mh3_fp8_attention_fwd/").  NVTX3 is
+// header-only: without an attached tool a push/pop is a pointer check, and
+// the library gains no link dependency.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 }  // namespace mh3

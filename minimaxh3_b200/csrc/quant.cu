@@ -640,6 +640,7 @@ bool launch_bh_quant(const void* x, int32_t in_dtype, int64_t D, int64_t sb, int
 extern "C" int mh3_absmax_bh(const void* x, int32_t in_dtype, int64_t B, int64_t S, int64_t H, int64_t D, int64_t sb,
                              int64_t ss, int64_t sh, int32_t head_block, int32_t head_off, int32_t heads_sel,
                              float* amax, void* stream) {
+  const mh3::NvtxRange nvtx_range("mh3_absmax_bh");
   const char* why = nullptr;
   if (!bh_shape_ok(x, in_dtype, B, S, H, D, sb, ss, sh, &why)) return fail(MH3_ERR_INVALID, (std::string("mh3_absmax_bh: ") + why).c_str());
   if (amax == nullptr) return fail(MH3_ERR_INVALID, "mh3_absmax_bh: null amax");
@@ -668,6 +669,7 @@ extern "C" int mh3_absmax_bh(const void* x, int32_t in_dtype, int64_t B, int64_t
 extern "C" int mh3_quantize_bh(const void* x, int32_t in_dtype, int64_t B, int64_t S, int64_t H, int64_t D, int64_t sb,
                                int64_t ss, int64_t sh, int32_t head_block, int32_t head_off, int32_t heads_sel,
                                const float* scale, int32_t out_dtype, void* out, void* stream) {
+  const mh3::NvtxRange nvtx_range("mh3_quantize_bh");
   const char* why = nullptr;
   if (!bh_shape_ok(x, in_dtype, B, S, H, D, sb, ss, sh, &why)) return fail(MH3_ERR_INVALID, (std::string("mh3_quantize_bh: ") + why).c_str());
   if (scale == nullptr || out == nullptr) return fail(MH3_ERR_INVALID, "mh3_quantize_bh: null scale or out");
@@ -689,6 +691,7 @@ extern "C" int mh3_quantize_bh(const void* x, int32_t in_dtype, int64_t B, int64
 extern "C" int mh3_absmax_seg(const void* x, int32_t in_dtype, int64_t S, int64_t H, int64_t D, int64_t ss,
                               int64_t sh, int32_t head_block, int32_t head_off, int32_t heads_sel, const int32_t* seg,
                               int32_t nseg, float* amax, void* stream) {
+  const mh3::NvtxRange nvtx_range("mh3_absmax_seg");
   const char* why = nullptr;
   if (!bh_shape_ok(x, in_dtype, 1, S, H, D, 0, ss, sh, &why)) return fail(MH3_ERR_INVALID, (std::string("mh3_absmax_seg: ") + why).c_str());
   if (amax == nullptr || seg == nullptr) return fail(MH3_ERR_INVALID, "mh3_absmax_seg: null amax or seg");
@@ -721,6 +724,7 @@ extern "C" int mh3_quantize_seg(const void* x, int32_t in_dtype, int64_t S, int6
                                 int64_t sh, int32_t head_block, int32_t head_off, int32_t heads_sel,
                                 const int32_t* seg, int32_t nseg, const float* scale, int32_t out_dtype, void* out,
                                 void* stream) {
+  const mh3::NvtxRange nvtx_range("mh3_quantize_seg");
   const char* why = nullptr;
   if (!bh_shape_ok(x, in_dtype, 1, S, H, D, 0, ss, sh, &why)) return fail(MH3_ERR_INVALID, (std::string("mh3_quantize_seg: ") + why).c_str());
   if (scale == nullptr || out == nullptr || seg == nullptr)
@@ -748,6 +752,7 @@ extern "C" uint64_t mh3_qkv_workspace_bytes(int32_t batch, int32_t heads, int32_
 }
 
 extern "C" int mh3_quantize_qkv(const mh3_qkv_quant_args* a, void* stream) {
+  const mh3::NvtxRange nvtx_range("mh3_quantize_qkv");
   if (a == nullptr) return fail(MH3_ERR_INVALID, "mh3_quantize_qkv: null args");
   if (a->head_dim != 64 && a->head_dim != 128) return fail(MH3_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
   if (a->batch <= 0 || a->heads <= 0 || a->seqlen_q <= 0 || a->seqlen_k <= 0)
@@ -780,6 +785,7 @@ extern "C" int mh3_quantize_qkv(const mh3_qkv_quant_args* a, void* stream) {
 
 extern "C" int mh3_quantize_rows(const void* x, int64_t x_stride, int32_t in_dtype, int64_t M, int64_t K, void* x8,
                                  float* scale, void* stream) {
+  const mh3::NvtxRange nvtx_range("mh3_quantize_rows");
   if (M < 0 || K < 0) return fail(MH3_ERR_INVALID, "negative size");
   if (M == 0 || K == 0) return MH3_OK;
   if (!x || !x8 || !scale) return fail(MH3_ERR_INVALID, "null pointer");
@@ -805,6 +811,7 @@ extern "C" int mh3_quantize_rows(const void* x, int64_t x_stride, int32_t in_dty
 }
 
 extern "C" int mh3_widen_e4m3_to_f16(const void* src, void* dst, int64_t n, void* stream) {
+  const mh3::NvtxRange nvtx_range("mh3_widen_e4m3_to_f16");
   if (n < 0) return fail(MH3_ERR_INVALID, "negative size");
   if (n == 0) return MH3_OK;
   if (!src || !dst) return fail(MH3_ERR_INVALID, "null pointer");

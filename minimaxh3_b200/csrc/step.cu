@@ -140,6 +140,7 @@ extern "C" uint64_t mh3_step_diff_workspace_bytes(void) { return (uint64_t)step:
 
 extern "C" int mh3_step_diff(const void* h1, void* prev, int32_t dtype, int64_t n, int32_t copy, double* sums,
                              void* workspace, void* stream) {
+  const mh3::NvtxRange nvtx_range("mh3_step_diff");
   if (n < 0) return fail(MH3_ERR_INVALID, "mh3_step_diff: negative size");
   if (!sums || (n > 0 && (!h1 || !prev || !workspace))) return fail(MH3_ERR_INVALID, "mh3_step_diff: null pointer");
   if (((uintptr_t)h1 & 15u) || ((uintptr_t)prev & 15u) || ((uintptr_t)workspace & 15u))

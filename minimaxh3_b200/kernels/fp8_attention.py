@@ -90,6 +90,7 @@ def is_supported(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> bool:
     return _device_is_sm100(q.device)
 
 
+@_ops.nvtx("mh3.fp8_attention")
 def _fp8_attention_impl(q, k, v, scale, key_mask, key_bias, repair_tau):
     B, H, Sq, D = q.shape
     Sk = k.shape[2]
@@ -162,6 +163,7 @@ def _per_segment_scales(x, cu):
     return _ops.scale_from_absmax(_ops.absmax_seg(x, cu))                  # [nseq, H]
 
 
+@_ops.nvtx("mh3.fp8_attention_varlen")
 def _fp8_attention_varlen_impl(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, scale):
     D = q.shape[2]
     ls2 = (scale if scale is not None else 1.0 / math.sqrt(D)) * LOG2E

@@ -67,6 +67,8 @@ import threading
 import torch
 import torch.distributed as dist
 
+from .ops import nvtx
+
 LOG2E = 1.4426950408889634
 E4M3 = torch.float8_e4m3fn
 
@@ -324,6 +326,7 @@ def _packing(cu_seqlens, P, r, B, S_l, device):
     return _Packing(cu_seqlens, P, r, S_l, device)
 
 
+@nvtx("mh3.ulysses_attention")
 def ulysses_attention(q, k, v, group=None, scale=None, pv_dtype=torch.float16, attn_fn=None, events=None,
                       absmax_fn=None, quant_fn=None, head_groups=1, out=None, cu_seqlens=None, cross_kv=None,
                       exchange="nccl"):
