@@ -66,3 +66,24 @@ def test_ulysses_exchange_argument_is_checked_before_any_collective():
         ulysses_attention(x, x, x, exchange="peer", head_groups=2)
     with pytest.raises(ValueError):
         ulysses_attention(x, x, x, exchange="peer", cu_seqlens=[0, 8], cross_kv=(x, x))
+
+
+def test_nvtx_range_decorator_is_transparent(monkeypatch):
+    """ops.nvtx pushes one range per call and pops it on return and on error."""
+    from minimaxh3_b200 import ops
+
+    calls = []
+    monkeypatch.setattr(torch.cuda.nvtx, "range_push", lambda name: calls.append(("push", name)))
+    monkeypatch.setattr(torch.cuda.nvtx, "range_pop", lambda: calls.append(("pop",)))
+
+    @ops.nvtx("mh3.test")
+    def f(x, y=1):
+        """doc"""
+        if x < 0:
+            raise ValueError("negative")
+        return x + y
+
+    assert f(2, y=3) == 5 and f.__name__ == "f" and f.__doc__ == "doc"
+    with pytest.raises(ValueError):
+        f(-1)
+    assert calls == [("push", "mh3.test"), ("pop",)] * 2
